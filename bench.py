@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 W4G64 QuantLinear forward (decode GEMV headline).
+
+Workload (BASELINE config 1 at M=1, i.e. one decode token through every
+quantised linear of Qwen2-1.5B): the seven linear shapes q 1536->1536,
+k/v 1536->256, o 1536->1536, gate/up 1536->8960, down 8960->1536, for each
+of the 28 layers, symmetric W4G64 RTN of bf16 weights ~N(0, 0.02), bf16
+activations ~N(0, 1), q/k/v with bf16 bias. A step is one pass over all 196
+linears; the 655 MB of packed weights per step are far larger than L2, so no
+flush is needed. Synthetic, seeded data (no checkpoint is used).
+
+  value  = algorithmic bytes per step (SURVEY 8d formula) / device time,
+           step captured once in a CUDA graph of C-ABI launches, replayed K times
+  e2e    = same metric through the public Python API (b200_w4g64_linear) with
+           the step's activations copied host->device and outputs device->host
+           inside the timed region
+  gemm   = the seven shapes at M=2048 (TFLOP/s), tensor-core kernel
+  roofline, cpu_baseline, clocks: see the JSON keys.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+Multi-GPU (torchrun): independent replicas, one per rank, weak scaling.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PACKAGE = "qwen2-int4-systems_b200"
+
+METRIC = "W4G64 GEMV HBM GB/s (M=1), GEMM TFLOP/s (M=2048); Qwen2-1.5B decode tok/s"
+UNIT = "GB/s"
+LAYERS = 28
+# (name, in_features K, out_features N, has_bias) - model.py:56-59,129-131
+SHAPES = [("q", 1536, 1536, True), ("k", 1536, 256, True), ("v", 1536, 256, True),
+          ("o", 1536, 1536, False), ("gate", 1536, 8960, False), ("up", 1536, 8960, False),
+          ("down", 8960, 1536, False)]
+WORKLOAD = "qwen2-1.5b-7-linears-x28-layers-w4g64-rtn-m1"
+
+
+def alg_bytes(m: int, n: int, k: int, bias: bool, asym: bool = False) -> int:
+    """Algorithmic bytes of one linear: packed weights + fp16 scales + x + out (+zeros, +bias)."""
+    b = n * k // 2 + n * (k // 64) * 2 + m * k * 2 + m * n * 2
+    if asym:
+        b += (n * (k // 64) + 1) // 2
+    if bias:
+        b += 2 * n
+    return b
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, sampled from a thread)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.period = period_s
+        self.handle = None
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            props = torch.cuda.get_device_properties(device_index)
+            uuid = str(getattr(props, "uuid", ""))
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                    uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+                idx = int(visible.split(",")[device_index]) if visible else device_index
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                sm = self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+                reasons = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((sm, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.handle is not None:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.handle is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s for s, _ in self.samples]
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [name for name, bit in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# synthetic weights (symmetric RTN of quantization.py:87-111, on the GPU)
+# ---------------------------------------------------------------------------
+
+def quantize_symmetric_rtn_gpu(n: int, k: int, gen: torch.Generator, device) -> tuple:
+    w = (torch.randn(n, k, device=device, generator=gen) * 0.02).to(torch.bfloat16).float()
+    g = w.view(n, k // 64, 64)
+    s = g.abs().amax(dim=-1) / 7.0
+    s = torch.where(s == 0, torch.ones_like(s), s)
+    codes = torch.round(g / s.unsqueeze(-1)).clamp_(-7, 7).to(torch.int16).view(n, k)
+    packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).reshape(-1, 1)
+    zeros = torch.zeros((n * (k // 64) + 1) // 2, 1, dtype=torch.uint8, device=device)
+    return packed.contiguous(), s.to(torch.float16).contiguous(), zeros
+
+
+def build_model_weights(device, seed: int = 0) -> list[list[dict]]:
+    gen = torch.Generator(device=device).manual_seed(seed)
+    layers = []
+    for _ in range(LAYERS):
+        layer = []
+        for name, k, n, has_bias in SHAPES:
+            qw, sc, z = quantize_symmetric_rtn_gpu(n, k, gen, device)
+            bias = (torch.randn(n, device=device, generator=gen) * 0.02).to(torch.bfloat16) if has_bias else None
+            layer.append({"name": name, "k": k, "n": n, "qweight": qw, "scales": sc, "zeros": z, "bias": bias})
+        layers.append(layer)
+    return layers
+
+
+# ---------------------------------------------------------------------------
+# device-side measurement through the C ABI
+# ---------------------------------------------------------------------------
+
+class Chain:
+    """A list of C-ABI launches with preallocated activations and outputs."""
+
+    def __init__(self, lib, entries: list[dict], m: int, device, gen: torch.Generator, algo: int = 0):
+        self.lib, self.entries, self.m, self.algo = lib, entries, m, algo
+        self.x = [torch.randn(m, e["k"], device=device, generator=gen).to(torch.bfloat16) for e in entries]
+        self.out = [torch.empty(m, e["n"], device=device, dtype=torch.bfloat16) for e in entries]
+
+    def launch(self):
+        stream = torch.cuda.current_stream().cuda_stream
+        for e, x, o in zip(self.entries, self.x, self.out):
+            b = e["bias"]
+            rc = self.lib.qi4_w4g64_linear_ex(
+                x.data_ptr(), 1, self.m, e["k"], e["qweight"].data_ptr(), e["scales"].data_ptr(),
+                e["zeros"].data_ptr(), None if b is None else b.data_ptr(), -1 if b is None else 1,
+                o.data_ptr(), e["n"], stream, self.algo, 1)
+            if rc:
+                raise RuntimeError(f"launch failed: {rc}")
+
+    def graph(self) -> torch.cuda.CUDAGraph:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.launch()
+            self.launch()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.launch()
+        return g
+
+    def bytes(self) -> int:
+        return sum(alg_bytes(self.m, e["n"], e["k"], e["bias"] is not None) for e in self.entries)
+
+    def flops(self) -> int:
+        return sum(2 * self.m * e["n"] * e["k"] for e in self.entries)
+
+
+def time_graph(g: torch.cuda.CUDAGraph, reps: int, warmup: int) -> float:
+    """Average ms per replay (CUDA events on the replay stream)."""
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        g.replay()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's torch backend restated (oracle/torch_port.py)
+# ---------------------------------------------------------------------------
+
+def cpu_linear_sample(reps: int = 3, sample: str = "layer") -> dict:
+    from oracle import torch_port
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(1)
+    shapes = SHAPES if sample == "layer" else [s for s in SHAPES if s[0] == "gate"]
+    data = []
+    for name, k, n, has_bias in shapes:
+        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).float().view(n, k // 64, 64)
+        s = w.abs().amax(-1) / 7.0
+        s = torch.where(s == 0, torch.ones_like(s), s)
+        codes = torch.round(w / s.unsqueeze(-1)).clamp_(-7, 7).to(torch.int16).view(n, k)
+        qw = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).reshape(-1, 1)
+        z = torch.zeros((n * (k // 64) + 1) // 2, 1, dtype=torch.uint8)
+        bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16) if has_bias else None
+        x = torch.randn(1, k, generator=gen).to(torch.bfloat16)
+        data.append((x, qw, s.to(torch.float16), z, bias, n, k))
+
+    def run():
+        for x, qw, sc, z, bias, n, k in data:
+            torch_port.linear(x, qw, sc, z, bias, out_features=n, in_features=k)
+
+    run()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    nbytes = sum(alg_bytes(1, n, k, bias is not None) for _, _, _, _, bias, n, k in data)
+    t = statistics.median(times)
+    return {"value": nbytes / t / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(data)} linear(s) of one layer at M=1 ({sample}), median of {reps}, "
+                      f"oracle/torch_port.py (reference torch backend restated) on {threads} threads",
+            "seconds_per_sample": t}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import torch_port  # noqa: F401  (fails loudly if the oracle is missing)
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(1)
+    per_step = []
+    for name, k, n, has_bias in SHAPES:
+        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).float().view(n, k // 64, 64)
+        s = w.abs().amax(-1) / 7.0
+        s = torch.where(s == 0, torch.ones_like(s), s)
+        codes = torch.round(w / s.unsqueeze(-1)).clamp_(-7, 7).to(torch.int16).view(n, k)
+        qw = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).reshape(-1, 1)
+        z = torch.zeros((n * (k // 64) + 1) // 2, 1, dtype=torch.uint8)
+        bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16) if has_bias else None
+        per_step.append((torch.randn(1, k, generator=gen).to(torch.bfloat16), qw, s.to(torch.float16), z,
+                         bias, n, k))
+    from oracle import torch_port as tp
+
+    def step():
+        for x, qw, sc, z, bias, n, k in per_step:
+            tp.linear(x, qw, sc, z, bias, out_features=n, in_features=k)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - t0
+    nbytes = sum(alg_bytes(1, n, k, bias is not None) for _, _, _, _, bias, n, k in per_step)
+    value = nbytes * args.steps / elapsed / 1e9
+    sample = (f"one layer's 7 linears at M=1 per step (1/28 of the GPU step), "
+              f"oracle/torch_port.py on {threads} host threads")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "m": 1, "sample": "1 of 28 layers"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+# ---------------------------------------------------------------------------
+# main (our arm)
+# ---------------------------------------------------------------------------
+
+def load_traffic() -> dict:
+    path = ROOT / "profiles" / "traffic.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-gemm", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+
+    pkg = importlib.import_module(PACKAGE)
+    lib = importlib.import_module(PACKAGE + "._lib").load()
+    layers = build_model_weights(device, seed=1234 + rank)
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    entries = [e for layer in layers for e in layer]
+    step_chain = Chain(lib, entries, 1, device, gen)
+    step_graph = step_chain.graph()
+    step_bytes = step_chain.bytes()
+    launches_per_step = len(entries)
+
+    # Timed region: K replays of the step graph, barrier + sync on both sides.
+    for _ in range(args.warmup):
+        step_graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step_graph.replay()
+        end.record()
+        end.synchronize()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = step_bytes * world * args.steps / (ms / 1e3) / 1e9
+
+    # Dominant kernel: the gate GEMV at M=1, chained over the 28 layers.
+    per_shape = {}
+    for idx, (name, k, n, has_bias) in enumerate(SHAPES):
+        chain = Chain(lib, [layer[idx] for layer in layers], 1, device, gen)
+        g = chain.graph()
+        t = time_graph(g, reps=20, warmup=3)
+        per_shape[name] = {"m": 1, "us_per_launch": t * 1e3 / LAYERS,
+                           "GBps": chain.bytes() / (t / 1e3) / 1e9}
+    gate = per_shape["gate"]
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        peaks = json.loads(peaks_path.read_text())
+        hbm_peak, peak_src = float(peaks["hbm_gbs"]), "measured"
+        tensor_peak = float(peaks.get("bf16_tflops", 1590.0))
+    else:
+        hbm_peak, peak_src, tensor_peak = 6650.0, "fallback", 1590.0
+    traffic = load_traffic().get("gemv_gate_m1_bytes_per_launch")
+    roofline = {"bound": "hbm", "kernel": "w4g64_gemv_kernel (gate 1536->8960, M=1)",
+                "achieved": gate["GBps"], "peak": hbm_peak, "unit": "GB/s",
+                "frac": gate["GBps"] / hbm_peak, "peak_source": peak_src,
+                "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False)}
+
+    # GEMM at M=2048 (tensor-core kernel) over one layer's seven shapes.
+    gemm = None
+    if not args.no_gemm:
+        gemm = {"m": 2048, "per_shape": {}}
+        total_flops, total_ms = 0, 0.0
+        for idx, (name, k, n, has_bias) in enumerate(SHAPES):
+            chain = Chain(lib, [layers[i][idx] for i in range(4)], 2048, device, gen, algo=2)
+            try:
+                g = chain.graph()
+            except RuntimeError:
+                gemm = None
+                break
+            t = time_graph(g, reps=10, warmup=3)
+            tf = chain.flops() / (t / 1e3) / 1e12
+            gemm["per_shape"][name] = {"TFLOPs": tf, "us_per_launch": t * 1e3 / 4}
+            total_flops += chain.flops()
+            total_ms += t
+        if gemm is not None:
+            gemm["TFLOPs_all_shapes"] = total_flops / (total_ms / 1e3) / 1e12
+            gemm["frac_of_bf16_peak"] = gemm["TFLOPs_all_shapes"] / tensor_peak
+
+    # End to end through the public API with host buffers.
+    x_host = torch.cat([x.view(-1) for x in step_chain.x]).cpu().pin_memory()
+    out_host = torch.empty(sum(e["n"] for e in entries), dtype=torch.bfloat16).pin_memory()
+    offsets, off = [], 0
+    for e in entries:
+        offsets.append(off)
+        off += e["k"]
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        outs = []
+        for e, o in zip(entries, offsets):
+            outs.append(pkg.b200_w4g64_linear(
+                xd[o:o + e["k"]].view(1, e["k"]), e["qweight"], e["scales"], e["zeros"], e["bias"],
+                out_features=e["n"], in_features=e["k"], group_size=64, packing="canonical"))
+        out_host.copy_(torch.cat([t.view(-1) for t in outs]), non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record()
+    ee.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e2e_steps
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": step_bytes * world / (e2e_ms / 1e3) / 1e9, "unit": UNIT,
+           "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
+           "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python, ctypes C-ABI)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_linear_sample()
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init W4G64 RTN weights)",
+        "config": {"workload": WORKLOAD, "m": 1, "layers": LAYERS, "linears_per_step": launches_per_step,
+                   "bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": roofline, "per_shape_m1": per_shape, "gemm_m2048": gemm,
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
+    }))
+
+
+if __name__ == "__main__":
+    main()

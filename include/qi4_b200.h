@@ -1,0 +1,124 @@
+/*
+ * qi4_b200.h - C ABI of the B200 (sm_100a) W4G64 QuantLinear backend.
+ *
+ * The library replaces the GPU side of the reference project
+ * ryanyue-16/qwen2-int4-systems (paths below are relative to its root):
+ * the dispatch target of QuantLinear.forward (src/qwen_int4/linear.py:56-72)
+ * and the Triton operators behind it (src/qwen_int4/triton_kernels.py).
+ *
+ * Checkpoint contract read unchanged (src/qwen_int4/linear.py:39-44,
+ * src/qwen_int4/quantization.py:30-84,221-258):
+ *   qweight  uint8  N*K/2 bytes, row-major [N, K/2]; element k of row n sits
+ *                   in byte (n*K + k)/2, low nibble for even k; signed INT4.
+ *   scales   fp16   [N, K/64], one scale per row and 64-wide K group.
+ *   zeros    uint8  (N*(K/64)+1)/2 bytes; signed INT4 zero point of
+ *                   (row n, group g) is nibble (n*G+g)&1 of byte (n*G+g)/2.
+ *                   NULL means all zero points are 0 (symmetric RTN).
+ *   W[n,k] = (code[n,k] - zero[n,k/64]) * scale[n,k/64]
+ *
+ * Conventions: every pointer is a device pointer borrowed from the caller;
+ * `stream` is a cudaStream_t (NULL = legacy default stream); calls only
+ * enqueue work and never synchronise. Return value 0 means success; a
+ * negative QI4_ERR_* code means nothing was launched (argument errors) or the
+ * launch failed; qi4_last_error() then gives a message. No C++ exception
+ * crosses this boundary. Calls on distinct streams may run concurrently.
+ */
+#ifndef QI4_B200_H
+#define QI4_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QI4_API __attribute__((visibility("default")))
+#else
+#define QI4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of activations, bias and outputs. */
+#define QI4_DTYPE_NONE (-1)
+#define QI4_DTYPE_F16 0
+#define QI4_DTYPE_BF16 1
+#define QI4_DTYPE_F32 2
+
+/* Status codes. */
+#define QI4_OK 0
+#define QI4_ERR_ARGUMENT (-1)  /* null pointer or non-positive size */
+#define QI4_ERR_DTYPE (-2)     /* unsupported element type */
+#define QI4_ERR_SHAPE (-3)     /* K not a multiple of 64, size limits */
+#define QI4_ERR_ALIGNMENT (-4) /* pointer alignment the kernels need */
+#define QI4_ERR_LAUNCH (-5)    /* CUDA launch / runtime error */
+#define QI4_ERR_DEVICE (-6)    /* current device is not sm_100 */
+
+/* Kernel choice for qi4_w4g64_linear_ex. */
+#define QI4_ALGO_AUTO 0 /* GEMV for small M, tensor-core GEMM otherwise */
+#define QI4_ALGO_GEMV 1 /* CUDA-core fused dequant GEMV (M <= 16) */
+#define QI4_ALGO_TC 2   /* tcgen05 dequant-GEMM with TMEM accumulators */
+
+/*
+ * out[M, N] = x[M, K] @ W^T (+ bias[N]), FP32 accumulation, bias added in
+ * FP32, result cast to x's dtype - the semantics of torch_reference_linear
+ * (src/qwen_int4/backends.py:73-98) and of linear_canonical_w4g64_triton
+ * (src/qwen_int4/triton_kernels.py:206-268).
+ *   x        [M, K] row-major, dtype x_dtype (F16, BF16 or F32), 16-byte aligned
+ *   qweight  16-byte aligned; scales 2-byte aligned
+ *   bias     [N] of bias_dtype (F16/BF16/F32) or NULL with QI4_DTYPE_NONE
+ *   out      [M, N] row-major, same dtype as x
+ * K must be a positive multiple of 64; M, N positive.
+ */
+QI4_API int qi4_w4g64_linear(const void* x, int x_dtype, int64_t M, int64_t K,
+                     const uint8_t* qweight, const uint16_t* scales_f16,
+                     const uint8_t* zeros, const void* bias, int bias_dtype,
+                     void* out, int64_t N, void* stream);
+
+/* Same as qi4_w4g64_linear with an explicit kernel choice (QI4_ALGO_*) and
+ * programmatic dependent launch on (pdl=1) or off (pdl=0). */
+QI4_API int qi4_w4g64_linear_ex(const void* x, int x_dtype, int64_t M, int64_t K,
+                        const uint8_t* qweight, const uint16_t* scales_f16,
+                        const uint8_t* zeros, const void* bias, int bias_dtype,
+                        void* out, int64_t N, void* stream, int algo, int pdl);
+
+/*
+ * out[N, K] = FP32 dequantised weight, bit-exact with dequantize_groupwise
+ * (src/qwen_int4/quantization.py:221-258) and
+ * dequantize_canonical_w4g64_triton (src/qwen_int4/triton_kernels.py:149-203).
+ * out must be 16-byte aligned.
+ */
+QI4_API int qi4_w4g64_dequant_f32(const uint8_t* qweight, const uint16_t* scales_f16,
+                          const uint8_t* zeros, float* out, int64_t N,
+                          int64_t K, void* stream);
+
+/*
+ * out[i] = signed INT4 element i of `packed` (even i from the low nibble),
+ * for 0 <= i < elements <= 2 * bytes; matches unpack_int4 CANONICAL
+ * (src/qwen_int4/quantization.py:53-84) and
+ * unpack_canonical_signed_int4_triton (src/qwen_int4/triton_kernels.py:119-146).
+ * elements == 0 is a no-op.
+ */
+QI4_API int qi4_w4_unpack(const uint8_t* packed, int8_t* out, int64_t elements,
+                  void* stream);
+
+/* Tuning hook: forces the decode-GEMV launch shape for subsequent calls made
+ * by the calling thread - lanes per weight row (8/16/32), warps per CTA,
+ * K-split factor (CTAs per cluster, 1..8) and per-lane load depth (4 or 8).
+ * lanes_per_row = 0 restores the library's own choice. No reference
+ * counterpart (the reference's Triton tile is a wrapper argument,
+ * src/qwen_int4/triton_kernels.py:213-216). */
+QI4_API int qi4_gemv_plan_override(int lanes_per_row, int warps, int ksplit, int depth);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to len) and returns its full length; 0 if no error was recorded. */
+QI4_API int qi4_last_error(char* buf, size_t len);
+
+/* ABI version of this header (major * 100 + minor). */
+QI4_API int qi4_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QI4_B200_H */

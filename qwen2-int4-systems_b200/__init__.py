@@ -1,0 +1,25 @@
+"""B200 (sm_100a) backend for the canonical W4G64 QuantLinear forward.
+
+Drop-in ``b200`` backend for ryanyue-16/qwen2-int4-systems: hand-written CUDA
+kernels behind the C ABI ``libqi4_b200.so`` (include/qi4_b200.h), called from
+PyTorch through ctypes. The directory name is not a Python identifier, so
+import it with ``importlib.import_module("qwen2-int4-systems_b200")``.
+"""
+
+from ._lib import ALGO_AUTO, ALGO_GEMV, ALGO_TC
+from .backends import (
+    SUPPORTED_BACKENDS,
+    b200_w4g64_linear,
+    dequantize_canonical_w4g64_b200,
+    linear_canonical_w4g64_b200,
+    set_value_checks,
+    unpack_canonical_signed_int4_b200,
+)
+from .integration import register_with_reference
+from .linear import QuantLinear
+
+__all__ = [
+    "ALGO_AUTO", "ALGO_GEMV", "ALGO_TC", "QuantLinear", "SUPPORTED_BACKENDS",
+    "b200_w4g64_linear", "dequantize_canonical_w4g64_b200", "linear_canonical_w4g64_b200",
+    "register_with_reference", "set_value_checks", "unpack_canonical_signed_int4_b200",
+]

@@ -1,0 +1,73 @@
+"""ctypes binding of ``libqi4_b200.so`` (the C ABI declared in include/qi4_b200.h).
+
+The library is loaded from this package directory. There is no fallback:
+if it is missing or cannot be loaded, every entry point raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqi4_b200.so"
+
+DTYPE_NONE, DTYPE_F16, DTYPE_BF16, DTYPE_F32 = -1, 0, 1, 2
+ALGO_AUTO, ALGO_GEMV, ALGO_TC = 0, 1, 2
+STATUS = {
+    -1: "ARGUMENT", -2: "DTYPE", -3: "SHAPE", -4: "ALIGNMENT", -5: "LAUNCH", -6: "DEVICE",
+}
+
+# Entry points and their C signatures (must match include/qi4_b200.h).
+_p, _i, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+SIGNATURES = {
+    "qi4_w4g64_linear": [_p, _i, _i64, _i64, _p, _p, _p, _p, _i, _p, _i64, _p],
+    "qi4_w4g64_linear_ex": [_p, _i, _i64, _i64, _p, _p, _p, _p, _i, _p, _i64, _p, _i, _i],
+    "qi4_w4g64_dequant_f32": [_p, _p, _p, _p, _i64, _i64, _p],
+    "qi4_w4_unpack": [_p, _p, _i64, _p],
+    "qi4_gemv_plan_override": [_i, _i, _i, _i],
+    "qi4_last_error": [ctypes.c_char_p, _sz],
+    "qi4_version": [],
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library once; raise RuntimeError if it is unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"B200 backend library {LIB_PATH.name} is not built; run the package's "
+                    "build step (build.py) - there is no CPU fallback")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    lib = load()
+    buf = ctypes.create_string_buffer(1024)
+    lib.qi4_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    """Turn a negative status into a Python exception with the library's message."""
+    if rc == 0:
+        return
+    message = f"{what} failed ({STATUS.get(rc, rc)}): {last_error()}"
+    if rc in (-1, -3, -4):
+        raise ValueError(message)
+    if rc == -2:
+        raise TypeError(message)
+    raise RuntimeError(message)

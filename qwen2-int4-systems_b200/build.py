@@ -1,0 +1,98 @@
+"""Build ``libqi4_b200.so`` (the C-ABI backend) in-tree with nvcc for sm_100a.
+
+    python -m <package>.build          # or: python qwen2-int4-systems_b200/build.py
+
+Objects go to ``_build/`` at the repository root; the shared library is
+written next to this file so that it travels with the source tree. Rebuilds
+only what changed (source or header newer than its object).
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = ROOT / "_build"
+LIB = PKG / "libqi4_b200.so"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O3,-fvisibility=hidden", "-Xptxas", "-v",
+    "-I", str(ROOT / "include"), "-I", str(CSRC),
+    "--expt-relaxed-constexpr",
+]
+# Only the extern "C" entry points are exported.
+EXPORTS = [
+    "qi4_w4g64_linear", "qi4_w4g64_linear_ex", "qi4_w4g64_dequant_f32",
+    "qi4_w4_unpack", "qi4_gemv_plan_override", "qi4_last_error", "qi4_version",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("CUDA_HOME", ""), "/usr/local/cuda"):
+        if cand and (Path(cand) / "bin" / "nvcc").exists():
+            return str(Path(cand) / "bin" / "nvcc")
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found; the B200 backend needs the CUDA toolkit to build")
+    return found
+
+
+def _sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def _headers() -> list[Path]:
+    return sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
+
+
+def _compile(src: Path, obj: Path, log: Path) -> None:
+    cmd = [nvcc(), *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    log.write_text(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{proc.stdout}{proc.stderr}")
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    newest_header = max((h.stat().st_mtime for h in _headers()), default=0.0)
+    jobs = []
+    objects = []
+    for src in _sources():
+        obj = BUILD / (src.stem + ".o")
+        objects.append(obj)
+        stale = (force or not obj.exists()
+                 or obj.stat().st_mtime < max(src.stat().st_mtime, newest_header))
+        if stale:
+            jobs.append((src, obj, BUILD / (src.stem + ".log")))
+    if jobs:
+        with ThreadPoolExecutor(max_workers=min(8, len(jobs))) as pool:
+            list(pool.map(lambda j: _compile(*j), jobs))
+        if verbose:
+            for _, _, log in jobs:
+                print(log.read_text())
+    link_needed = force or jobs or not LIB.exists() or any(
+        o.stat().st_mtime > LIB.stat().st_mtime for o in objects)
+    if link_needed:
+        tmp = LIB.with_suffix(".so.tmp")
+        cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp),
+               *map(str, objects), "-lcudart_static", "-lrt", "-ldl", "-lpthread"]
+        proc = subprocess.run(cmd, capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise RuntimeError(f"link failed:\n{proc.stdout}{proc.stderr}")
+        os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    path = build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+    print(path)

@@ -1,0 +1,284 @@
+// extern "C" boundary of libqi4_b200.so (declared in include/qi4_b200.h).
+//
+// Validates arguments, checks the device, picks a kernel and launches it on
+// the caller's stream. Nothing here allocates device memory or synchronises.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "dequant.cuh"
+#include "gemm_tc.cuh"
+#include "gemv.cuh"
+#include "qi4_common.cuh"
+
+namespace qi4 {
+
+namespace {
+thread_local std::string g_last_error;
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool ok = false;
+};
+
+// Per-device properties, filled on first use.
+DeviceInfo device_info(int dev) {
+  static std::mutex mu;
+  static DeviceInfo cache[64];
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return DeviceInfo{};
+  if (!cache[dev].ok) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DeviceInfo{};
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return DeviceInfo{};
+    cache[dev] = DeviceInfo{sms, major, true};
+  }
+  return cache[dev];
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+bool valid_act_dtype(int d) { return d == QI4_DTYPE_F16 || d == QI4_DTYPE_BF16 || d == QI4_DTYPE_F32; }
+
+int current_device(DeviceInfo& info) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("no CUDA device is available");
+    return QI4_ERR_DEVICE;
+  }
+  info = device_info(dev);
+  if (!info.ok) {
+    set_error("cannot query CUDA device %d", dev);
+    return QI4_ERR_DEVICE;
+  }
+  if (info.major != 10) {
+    set_error("device %d has compute capability %d.x; this library is built for sm_100a (B200)", dev,
+              info.major);
+    return QI4_ERR_DEVICE;
+  }
+  return QI4_OK;
+}
+
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s launch failed: %s", what, cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
+  return QI4_OK;
+}
+
+static int check_launch(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s launch failed: %s", what, cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
+  return QI4_OK;
+}
+
+static int validate_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                           const uint16_t* scales, const void* bias, int bias_dtype, void* out, int64_t N) {
+  if (!x || !qweight || !scales || !out) {
+    set_error("x, qweight, scales and out must be non-null device pointers");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (M <= 0 || N <= 0 || K <= 0) {
+    set_error("M, N and K must be positive (got M=%lld N=%lld K=%lld)", (long long)M, (long long)N,
+              (long long)K);
+    return QI4_ERR_ARGUMENT;
+  }
+  if (K % kGroup) {
+    set_error("canonical W4G64 requires K divisible by 64 (got K=%lld)", (long long)K);
+    return QI4_ERR_SHAPE;
+  }
+  if (K > (int64_t)1 << 24 || N > (int64_t)1 << 30 || M > (int64_t)1 << 30) {
+    set_error("problem size out of range (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
+    return QI4_ERR_SHAPE;
+  }
+  if (!valid_act_dtype(x_dtype)) {
+    set_error("activation dtype code %d is not F16, BF16 or F32", x_dtype);
+    return QI4_ERR_DTYPE;
+  }
+  if (bias != nullptr && !valid_act_dtype(bias_dtype)) {
+    set_error("bias dtype code %d is not F16, BF16 or F32", bias_dtype);
+    return QI4_ERR_DTYPE;
+  }
+  if (!aligned(qweight, 16)) {
+    set_error("qweight must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  if (!aligned(x, 16)) {
+    set_error("x must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  if (!aligned(scales, 2) || !aligned(out, x_dtype == QI4_DTYPE_F32 ? 4 : 2)) {
+    set_error("scales / out are not naturally aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  return QI4_OK;
+}
+
+static int linear_impl(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                       const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
+                       int64_t N, void* stream_ptr, int algo, int pdl) {
+  clear_error();
+  int rc = validate_linear(x, x_dtype, M, K, qweight, scales, bias, bias_dtype, out, N);
+  if (rc) return rc;
+  DeviceInfo info;
+  rc = current_device(info);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (!bias) bias_dtype = QI4_DTYPE_NONE;
+
+  if (algo == QI4_ALGO_AUTO) {
+    algo = (M > kGemvMaxM && tc_supported(M, N, K, x_dtype)) ? QI4_ALGO_TC : QI4_ALGO_GEMV;
+  } else if (algo == QI4_ALGO_TC && !tc_supported(M, N, K, x_dtype)) {
+    set_error("the tensor-core kernel does not support M=%lld N=%lld K=%lld dtype=%d", (long long)M,
+              (long long)N, (long long)K, x_dtype);
+    return QI4_ERR_SHAPE;
+  }
+
+  if (algo == QI4_ALGO_TC) {
+    return check_launch(launch_gemm_tc(x, x_dtype, M, K, qweight, scales, zeros, bias, bias_dtype, out, N, stream,
+                                       pdl != 0, info.sms),
+                        "w4g64 tcgen05 GEMM");
+  }
+  if (algo != QI4_ALGO_GEMV) {
+    set_error("unknown algorithm code %d", algo);
+    return QI4_ERR_ARGUMENT;
+  }
+  // The GEMV covers up to 16 token rows per launch; larger M is processed in
+  // row blocks (each block re-streams the weights).
+  const size_t xsize = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
+  for (int64_t m0 = 0; m0 < M; m0 += kGemvMaxM) {
+    const int64_t mb = (M - m0) < kGemvMaxM ? (M - m0) : kGemvMaxM;
+    const GemvPlan plan = plan_gemv(mb, N, K, info.sms);
+    if (plan.mt == 0) {
+      set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)N, (long long)K);
+      return QI4_ERR_SHAPE;
+    }
+    rc = check_launch(launch_gemv(static_cast<const char*>(x) + m0 * K * xsize, x_dtype, mb, K, qweight, scales,
+                                  zeros, bias, bias_dtype, static_cast<char*>(out) + m0 * N * xsize, N, stream,
+                                  pdl != 0, plan),
+                      "w4g64 GEMV");
+    if (rc) return rc;
+  }
+  return QI4_OK;
+}
+
+}  // namespace qi4
+
+using namespace qi4;
+
+extern "C" {
+
+int qi4_w4g64_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                     const uint16_t* scales_f16, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
+                     int64_t N, void* stream) {
+  return linear_impl(x, x_dtype, M, K, qweight, scales_f16, zeros, bias, bias_dtype, out, N, stream,
+                     QI4_ALGO_AUTO, 1);
+}
+
+int qi4_w4g64_linear_ex(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                        const uint16_t* scales_f16, const uint8_t* zeros, const void* bias, int bias_dtype,
+                        void* out, int64_t N, void* stream, int algo, int pdl) {
+  return linear_impl(x, x_dtype, M, K, qweight, scales_f16, zeros, bias, bias_dtype, out, N, stream, algo, pdl);
+}
+
+int qi4_w4g64_dequant_f32(const uint8_t* qweight, const uint16_t* scales_f16, const uint8_t* zeros, float* out,
+                          int64_t N, int64_t K, void* stream) {
+  clear_error();
+  if (!qweight || !scales_f16 || !out) {
+    set_error("qweight, scales and out must be non-null device pointers");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (N <= 0 || K <= 0) {
+    set_error("N and K must be positive");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (K % kGroup) {
+    set_error("canonical W4G64 dequantization requires K divisible by 64 (got K=%lld)", (long long)K);
+    return QI4_ERR_SHAPE;
+  }
+  if (!aligned(qweight, 16) || !aligned(out, 16) || !aligned(scales_f16, 2)) {
+    set_error("qweight and out must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  DeviceInfo info;
+  int rc = current_device(info);
+  if (rc) return rc;
+  return check_launch(launch_dequant_f32(qweight, scales_f16, zeros, out, N, K, static_cast<cudaStream_t>(stream),
+                                         info.sms),
+                      "w4g64 dequant");
+}
+
+int qi4_w4_unpack(const uint8_t* packed, int8_t* out, int64_t elements, void* stream) {
+  clear_error();
+  if (elements < 0) {
+    set_error("elements must be non-negative");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (elements == 0) return QI4_OK;
+  if (!packed || !out) {
+    set_error("packed and out must be non-null device pointers");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (!aligned(packed, 16) || !aligned(out, 16)) {
+    set_error("packed and out must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  DeviceInfo info;
+  int rc = current_device(info);
+  if (rc) return rc;
+  return check_launch(launch_unpack(packed, out, elements, static_cast<cudaStream_t>(stream), info.sms),
+                      "int4 unpack");
+}
+
+int qi4_gemv_plan_override(int lanes_per_row, int warps, int ksplit, int depth) {
+  clear_error();
+  if (lanes_per_row == 0) {
+    set_gemv_override(0, 0, 0, 0);
+    return QI4_OK;
+  }
+  const bool ok = (lanes_per_row == 8 || lanes_per_row == 16 || lanes_per_row == 32) &&
+                  (warps == 4 || warps == 8) && ksplit >= 1 && ksplit <= 8 && (depth == 4 || depth == 8);
+  if (!ok) {
+    set_error("invalid GEMV plan override (lanes_per_row %d, warps %d, ksplit %d, depth %d)", lanes_per_row,
+              warps, ksplit, depth);
+    return QI4_ERR_ARGUMENT;
+  }
+  set_gemv_override(lanes_per_row, warps, ksplit, depth);
+  return QI4_OK;
+}
+
+int qi4_last_error(char* buf, size_t len) {
+  const std::string& s = g_last_error;
+  if (buf && len) {
+    const size_t n = s.size() < len - 1 ? s.size() : len - 1;
+    memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+  }
+  return (int)s.size();
+}
+
+int qi4_version(void) { return 100; }
+
+}  // extern "C"

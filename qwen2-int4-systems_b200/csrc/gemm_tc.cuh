@@ -1,0 +1,16 @@
+// Host interface of the tcgen05 dequant-GEMM (gemm_tc.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qi4 {
+
+// Whether the tensor-core kernel handles this problem.
+bool tc_supported(int64_t M, int64_t N, int64_t K, int x_dtype);
+
+cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                           const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
+                           int64_t N, cudaStream_t stream, bool pdl, int num_sms);
+
+}  // namespace qi4

@@ -1,0 +1,46 @@
+"""Register the ``b200`` backend with the reference package at run time.
+
+The reference project ryanyue-16/qwen2-int4-systems selects a QuantLinear
+backend by name (src/qwen_int4/backends.py:11 ``SUPPORTED_BACKENDS``,
+src/qwen_int4/linear.py:51-72 ``set_backend`` / ``forward``,
+src/qwen_int4/cli.py:59 ``--backend`` choices). ``register_with_reference``
+adds ``"b200"`` to those tables in an already-imported ``qwen_int4`` package,
+so the unmodified model (src/qwen_int4/model.py) runs on the B200 kernels
+after ``model.set_backend("b200")``. The static patch a maintainer would
+commit instead is the three-line change shown in INTEGRATION.md.
+"""
+
+from __future__ import annotations
+
+import importlib
+
+from .backends import b200_w4g64_linear
+
+BACKEND = "b200"
+
+
+def register_with_reference(package: str = "qwen_int4") -> None:
+    """Make ``backend="b200"`` valid in the reference's QuantLinear. Idempotent."""
+    backends = importlib.import_module(f"{package}.backends")
+    linear = importlib.import_module(f"{package}.linear")
+    if BACKEND not in backends.SUPPORTED_BACKENDS:
+        backends.SUPPORTED_BACKENDS = tuple(backends.SUPPORTED_BACKENDS) + (BACKEND,)
+    # linear.py imported the tuple by name, so its binding is updated too.
+    linear.SUPPORTED_BACKENDS = backends.SUPPORTED_BACKENDS
+    backends.b200_w4g64_linear = b200_w4g64_linear
+    quant_linear = linear.QuantLinear
+    if getattr(quant_linear.forward, "_b200_dispatch", False):
+        return
+    reference_forward = quant_linear.forward
+
+    def forward(self, x):
+        if self.backend == BACKEND:
+            return b200_w4g64_linear(
+                x, self.qweight, self.scales, self.zeros, self.bias,
+                out_features=self.out_features, in_features=self.in_features,
+                group_size=self.group_size, packing=self.packing,
+            )
+        return reference_forward(self, x)
+
+    forward._b200_dispatch = True
+    quant_linear.forward = forward

@@ -1,0 +1,165 @@
+"""Host-side contract of the b200 backend (CPU only).
+
+Mirrors the fail-closed rejections of the reference's backend tests
+(ryanyue-16/qwen2-int4-systems tests/test_backends.py:178-270 and
+tests/test_triton_unpack.py:319-326,345-360,392-400): every bad input raises
+before any launch, with the same error class and message fragment.
+"""
+
+import sys
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import w4g64 as orc
+
+GROUP = 64
+
+
+def _tensors(n=6, k=128):
+    values = np.arange(n * k, dtype=np.float32)
+    w = ((np.remainder(values, 31) - 15) / 8).reshape(n, k)
+    qw, sc, z = orc.quantize_asymmetric_rtn(w)
+    return torch.from_numpy(qw), torch.from_numpy(sc), torch.from_numpy(z)
+
+
+def _call(b200, x, qw, sc, z, bias=None, **override):
+    args = {"out_features": 6, "in_features": 128, "group_size": GROUP, "packing": "canonical"}
+    args.update(override)
+    return b200.b200_w4g64_linear(x, qw, sc, z, bias, **args)
+
+
+@pytest.mark.parametrize(("override", "error", "message"), [
+    ({"group_size": 128}, ValueError, "W4G64"),
+    ({"packing": "legacy_signed_add"}, ValueError, "canonical INT4 packing"),
+    ({"in_features": 64}, ValueError, "activation feature dimension"),
+    ({"in_features": 96}, ValueError, "divisible by group size 64"),
+])
+def test_rejects_incompatible_mapping(b200, override, error, message):
+    qw, sc, z = _tensors()
+    with pytest.raises(error, match=message):
+        _call(b200, torch.ones(1, 128, dtype=torch.bfloat16), qw, sc, z, **override)
+
+
+@pytest.mark.parametrize("target", ["qweight", "scales", "zeros", "bias"])
+def test_rejects_inconsistent_tensor_shapes(b200, target):
+    qw, sc, z = _tensors()
+    tensors = {"qweight": qw, "scales": sc, "zeros": z, "bias": torch.zeros(6, dtype=torch.bfloat16)}
+    tensors[target] = tensors[target][:-1]
+    with pytest.raises(ValueError, match=target):
+        _call(b200, torch.ones(1, 128, dtype=torch.bfloat16), tensors["qweight"], tensors["scales"],
+              tensors["zeros"], tensors["bias"])
+
+
+@pytest.mark.parametrize(("mutation", "error", "message"), [
+    ("qweight_dtype", TypeError, "uint8"),
+    ("zeros_dtype", TypeError, "uint8"),
+    ("scales_dtype", TypeError, "FP16"),
+    ("x_dtype", TypeError, "FP16, BF16, or FP32"),
+])
+def test_rejects_malformed_dtypes(b200, mutation, error, message):
+    qw, sc, z = _tensors()
+    x = torch.ones(1, 128, dtype=torch.bfloat16)
+    if mutation == "qweight_dtype":
+        qw = qw.to(torch.int8)
+    elif mutation == "zeros_dtype":
+        z = z.to(torch.int8)
+    elif mutation == "scales_dtype":
+        sc = sc.to(torch.float32)
+    else:
+        x = x.to(torch.float64)
+    with pytest.raises(error, match=message):
+        _call(b200, x, qw, sc, z)
+
+
+def test_value_checks_reject_bad_scales_when_enabled(b200):
+    qw, sc, z = _tensors()
+    sc[0, 0] = float("nan")
+    b200.set_value_checks(True)
+    try:
+        # Value checks run after the device check, so on a CPU host the device
+        # error comes first; the flag itself must round-trip.
+        with pytest.raises(ValueError):
+            _call(b200, torch.ones(1, 128, dtype=torch.bfloat16), qw, sc, z)
+    finally:
+        b200.set_value_checks(False)
+
+
+def test_cpu_tensors_are_rejected_not_computed(b200):
+    qw, sc, z = _tensors()
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        _call(b200, torch.ones(1, 128, dtype=torch.bfloat16), qw, sc, z)
+
+
+def test_prims_reject_invalid_contracts_on_cpu_tensors(b200):
+    packed = torch.zeros(4, dtype=torch.uint8)
+    with pytest.raises((ValueError, RuntimeError)):
+        b200.unpack_canonical_signed_int4_b200(packed)
+    with pytest.raises((ValueError, RuntimeError)):
+        b200.dequantize_canonical_w4g64_b200(torch.zeros(64, dtype=torch.uint8),
+                                             torch.ones(2, dtype=torch.float16),
+                                             torch.zeros(1, dtype=torch.uint8),
+                                             out_features=1, in_features=96)
+
+
+def test_quantlinear_mirror_buffers_and_backend_selection(b200):
+    layer = b200.QuantLinear(1536, 256, group_size=64, bias=True)
+    assert layer.qweight.shape == (256 * 1536 // 2, 1) and layer.qweight.dtype == torch.uint8
+    assert layer.scales.shape == (256, 24) and layer.scales.dtype == torch.float16
+    assert layer.zeros.shape == ((256 * 24 + 1) // 2, 1)
+    assert layer.bias.dtype == torch.bfloat16
+    with pytest.raises(ValueError):
+        layer.set_backend("environment-variable-magic")
+    with pytest.raises(ValueError):
+        b200.QuantLinear(96, 4, group_size=64)
+
+
+def _fake_reference_package(name):
+    """A stand-in with the reference's dispatch structure (backends.py:11, linear.py:51-72)."""
+    pkg = types.ModuleType(name)
+    pkg.__path__ = []
+    backends = types.ModuleType(name + ".backends")
+    backends.SUPPORTED_BACKENDS = ("torch", "lpu", "triton")
+    backends.torch_reference_linear = lambda *a, **k: "torch"
+    linear = types.ModuleType(name + ".linear")
+    linear.SUPPORTED_BACKENDS = backends.SUPPORTED_BACKENDS
+
+    class QuantLinear(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.backend = "torch"
+
+        def set_backend(self, backend):
+            if backend not in linear.SUPPORTED_BACKENDS:
+                raise ValueError(f"unknown backend {backend!r}")
+            self.backend = backend
+
+        def forward(self, x):
+            return {"torch": backends.torch_reference_linear}[self.backend](x)
+
+    linear.QuantLinear = QuantLinear
+    sys.modules[name] = pkg
+    sys.modules[name + ".backends"] = backends
+    sys.modules[name + ".linear"] = linear
+    return backends, linear
+
+
+def test_register_with_reference_adds_explicit_backend(b200):
+    name = "fake_qwen_int4_for_registration"
+    backends, linear = _fake_reference_package(name)
+    try:
+        b200.register_with_reference(name)
+        b200.register_with_reference(name)  # idempotent
+        assert backends.SUPPORTED_BACKENDS.count("b200") == 1
+        assert linear.SUPPORTED_BACKENDS == backends.SUPPORTED_BACKENDS
+        layer = linear.QuantLinear()
+        assert layer(torch.zeros(1)) == "torch"  # other backends untouched
+        layer.set_backend("b200")
+        assert layer.backend == "b200"
+        with pytest.raises(ValueError):
+            layer.set_backend("b201")
+    finally:
+        for key in [k for k in sys.modules if k.startswith(name)]:
+            del sys.modules[key]
