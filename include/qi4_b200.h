@@ -56,8 +56,9 @@ extern "C" {
 
 /* Kernel choice for qi4_w4g64_linear_ex. */
 #define QI4_ALGO_AUTO 0 /* GEMV for small M, tensor-core GEMM otherwise */
-#define QI4_ALGO_GEMV 1 /* CUDA-core fused dequant GEMV (M <= 16) */
-#define QI4_ALGO_TC 2   /* tcgen05 dequant-GEMM with TMEM accumulators */
+#define QI4_ALGO_GEMV 1     /* TMA-staged, tensor-pipe decode GEMV (M <= 16) */
+#define QI4_ALGO_TC 2       /* tcgen05 dequant-GEMM with TMEM accumulators */
+#define QI4_ALGO_GEMV_FMA 3 /* CUDA-core FP32-FMA decode GEMV (M <= 16) */
 
 /*
  * out[M, N] = x[M, K] @ W^T (+ bias[N]), FP32 accumulation, bias added in
@@ -102,7 +103,20 @@ QI4_API int qi4_w4g64_dequant_f32(const uint8_t* qweight, const uint16_t* scales
 QI4_API int qi4_w4_unpack(const uint8_t* packed, int8_t* out, int64_t elements,
                   void* stream);
 
-/* Tuning hook: forces the decode-GEMV launch shape for subsequent calls made
+/* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
+ * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128) and
+ * K-split factor (CTAs per cluster, 1..8). rows = 0 restores the library's
+ * own choice. No reference counterpart. */
+QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit);
+
+/* Reads and clears the device-side error flags of the kernels (a bounded
+ * wait that timed out records QI4_DEVICE_WAIT_TIMEOUT). Synchronises
+ * `stream`. Returns the flags (0 = none) or a negative QI4_ERR_* code.
+ * No reference counterpart (the reference has no device-side waits). */
+#define QI4_DEVICE_WAIT_TIMEOUT 1
+QI4_API int qi4_device_status(void* stream);
+
+/* Tuning hook: forces the FP32-FMA decode-GEMV launch shape for subsequent calls made
  * by the calling thread - lanes per weight row (8/16/32), warps per CTA,
  * K-split factor (CTAs per cluster, 1..8) and per-lane load depth (4 or 8).
  * lanes_per_row = 0 restores the library's own choice. No reference

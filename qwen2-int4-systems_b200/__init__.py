@@ -6,7 +6,7 @@ PyTorch through ctypes. The directory name is not a Python identifier, so
 import it with ``importlib.import_module("qwen2-int4-systems_b200")``.
 """
 
-from ._lib import ALGO_AUTO, ALGO_GEMV, ALGO_TC
+from ._lib import ALGO_AUTO, ALGO_GEMV, ALGO_GEMV_FMA, ALGO_TC
 from .backends import (
     SUPPORTED_BACKENDS,
     b200_w4g64_linear,
@@ -19,7 +19,7 @@ from .integration import register_with_reference
 from .linear import QuantLinear
 
 __all__ = [
-    "ALGO_AUTO", "ALGO_GEMV", "ALGO_TC", "QuantLinear", "SUPPORTED_BACKENDS",
+    "ALGO_AUTO", "ALGO_GEMV", "ALGO_GEMV_FMA", "ALGO_TC", "QuantLinear", "SUPPORTED_BACKENDS",
     "b200_w4g64_linear", "dequantize_canonical_w4g64_b200", "linear_canonical_w4g64_b200",
     "register_with_reference", "set_value_checks", "unpack_canonical_signed_int4_b200",
 ]

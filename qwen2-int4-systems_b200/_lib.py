@@ -13,7 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libqi4_b200.so"
 
 DTYPE_NONE, DTYPE_F16, DTYPE_BF16, DTYPE_F32 = -1, 0, 1, 2
-ALGO_AUTO, ALGO_GEMV, ALGO_TC = 0, 1, 2
+ALGO_AUTO, ALGO_GEMV, ALGO_TC, ALGO_GEMV_FMA = 0, 1, 2, 3
 STATUS = {
     -1: "ARGUMENT", -2: "DTYPE", -3: "SHAPE", -4: "ALIGNMENT", -5: "LAUNCH", -6: "DEVICE",
 }
@@ -26,6 +26,8 @@ SIGNATURES = {
     "qi4_w4g64_dequant_f32": [_p, _p, _p, _p, _i64, _i64, _p],
     "qi4_w4_unpack": [_p, _p, _i64, _p],
     "qi4_gemv_plan_override": [_i, _i, _i, _i],
+    "qi4_gemv_mma_plan_override": [_i, _i],
+    "qi4_device_status": [_p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }

@@ -11,6 +11,7 @@
 #include "dequant.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
+#include "gemv_mma.cuh"
 #include "qi4_common.cuh"
 
 namespace qi4 {
@@ -161,24 +162,36 @@ static int linear_impl(const void* x, int x_dtype, int64_t M, int64_t K, const u
                                        pdl != 0, info.sms),
                         "w4g64 tcgen05 GEMM");
   }
-  if (algo != QI4_ALGO_GEMV) {
+  if (algo != QI4_ALGO_GEMV && algo != QI4_ALGO_GEMV_FMA) {
     set_error("unknown algorithm code %d", algo);
     return QI4_ERR_ARGUMENT;
   }
-  // The GEMV covers up to 16 token rows per launch; larger M is processed in
-  // row blocks (each block re-streams the weights).
+  // A GEMV launch covers up to 16 token rows; larger M is processed in row
+  // blocks (each block re-streams the weights).
   const size_t xsize = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
   for (int64_t m0 = 0; m0 < M; m0 += kGemvMaxM) {
     const int64_t mb = (M - m0) < kGemvMaxM ? (M - m0) : kGemvMaxM;
-    const GemvPlan plan = plan_gemv(mb, N, K, info.sms);
-    if (plan.mt == 0) {
-      set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)N, (long long)K);
-      return QI4_ERR_SHAPE;
+    const void* xb = static_cast<const char*>(x) + m0 * K * xsize;
+    void* ob = static_cast<char*>(out) + m0 * N * xsize;
+    if (algo == QI4_ALGO_GEMV) {
+      const MmaGemvPlan plan = plan_gemv_mma(mb, N, K, x_dtype, info.sms);
+      if (plan.rows == 0) {
+        set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)N, (long long)K);
+        return QI4_ERR_SHAPE;
+      }
+      rc = check_launch(
+          launch_gemv_mma(xb, x_dtype, mb, K, qweight, scales, zeros, bias, bias_dtype, ob, N, stream, pdl != 0, plan),
+          "w4g64 GEMV");
+    } else {
+      const GemvPlan plan = plan_gemv(mb, N, K, info.sms);
+      if (plan.mt == 0) {
+        set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)N, (long long)K);
+        return QI4_ERR_SHAPE;
+      }
+      rc = check_launch(
+          launch_gemv(xb, x_dtype, mb, K, qweight, scales, zeros, bias, bias_dtype, ob, N, stream, pdl != 0, plan),
+          "w4g64 FMA GEMV");
     }
-    rc = check_launch(launch_gemv(static_cast<const char*>(x) + m0 * K * xsize, x_dtype, mb, K, qweight, scales,
-                                  zeros, bias, bias_dtype, static_cast<char*>(out) + m0 * N * xsize, N, stream,
-                                  pdl != 0, plan),
-                      "w4g64 GEMV");
     if (rc) return rc;
   }
   return QI4_OK;
@@ -267,6 +280,30 @@ int qi4_gemv_plan_override(int lanes_per_row, int warps, int ksplit, int depth) 
   }
   set_gemv_override(lanes_per_row, warps, ksplit, depth);
   return QI4_OK;
+}
+
+int qi4_gemv_mma_plan_override(int rows, int ksplit) {
+  clear_error();
+  if (rows == 0) {
+    set_gemv_mma_override(0, 0);
+    return QI4_OK;
+  }
+  if ((rows != 16 && rows != 32 && rows != 64 && rows != 128) || ksplit < 1 || ksplit > 8) {
+    set_error("invalid GEMV plan override (rows %d, ksplit %d)", rows, ksplit);
+    return QI4_ERR_ARGUMENT;
+  }
+  set_gemv_mma_override(rows, ksplit);
+  return QI4_OK;
+}
+
+int qi4_device_status(void* stream) {
+  clear_error();
+  const int v = read_gemv_mma_error(static_cast<cudaStream_t>(stream));
+  if (v < 0) {
+    set_error("cannot read the device error flags: %s", cudaGetErrorString(cudaGetLastError()));
+    return QI4_ERR_LAUNCH;
+  }
+  return v;
 }
 
 int qi4_last_error(char* buf, size_t len) {

@@ -1,0 +1,27 @@
+// Host interface of the TMA + tensor-core decode GEMV (gemv_mma.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qi4 {
+
+struct MmaGemvPlan {
+  int rows;             // output rows per CTA: 16, 32 or 64
+  int ksplit;           // CTAs per cluster along K (1..8)
+  int boxes_per_split;  // 128-byte (4-group) boxes of K per CTA
+  int nt;               // n8 token tiles: 1 (M <= 8) or 2 (M <= 16)
+  size_t smem;
+};
+
+bool gemv_mma_supported(int64_t M, int64_t K);
+MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms);
+void set_gemv_mma_override(int rows, int ksplit);  // rows = 0 restores the model
+cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
+                            void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& plan);
+// Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
+int read_gemv_mma_error(cudaStream_t stream);
+
+}  // namespace qi4

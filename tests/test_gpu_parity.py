@@ -22,7 +22,7 @@ import _golden as G
 
 pytestmark = pytest.mark.gpu
 
-ALGOS = {"auto": 0, "gemv": 1}
+ALGOS = {"auto": 0, "gemv": 1, "gemv_fma": 3}
 
 
 def _ulp(ref: np.ndarray, dtype: torch.dtype) -> np.ndarray:
@@ -188,9 +188,10 @@ def _weights(k, n, kind, seed):
     return _WCACHE[key]
 
 
+@pytest.mark.parametrize("algo", ["gemv", "gemv_fma"])
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 13, 16])
 @pytest.mark.parametrize("name", list(QWEN_SHAPES))
-def test_gemv_shape_sweep(b200, cuda_device, name, m):
+def test_gemv_shape_sweep(b200, cuda_device, name, m, algo):
     k, n = QWEN_SHAPES[name]
     qw, sc, z = _weights(k, n, "sym", 11)
     g = torch.Generator().manual_seed(1000 + m)
@@ -199,26 +200,27 @@ def test_gemv_shape_sweep(b200, cuda_device, name, m):
     got = b200.b200_w4g64_linear(
         x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device),
         None if bias is None else bias.to(cuda_device), out_features=n, in_features=k, group_size=64,
-        packing="canonical", algo=ALGOS["gemv"])
+        packing="canonical", algo=ALGOS[algo])
     ref = orc.linear(x.float().numpy(), qw, sc, z, None if bias is None else bias.float().numpy(),
                      out_features=n, in_features=k, accumulate="f64")
-    assert_linear_close(got, ref, 1e-3, f"{name} m={m}")
+    assert_linear_close(got, ref, 1e-3, f"{name} m={m} {algo}")
 
 
+@pytest.mark.parametrize("algo", ["gemv", "gemv_fma"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("m", [1, 16])
-def test_gemv_awq_down_proj_all_dtypes(b200, cuda_device, dtype, m):
+def test_gemv_awq_down_proj_all_dtypes(b200, cuda_device, dtype, m, algo):
     qw, sc, z = G.cfg2_weights()
     chan = torch.from_numpy(G.arrays()["cfg2_chan"])
     g = torch.Generator().manual_seed(300 + m)
     x = (torch.randn(m, 8960, generator=g) / chan).to(dtype)
     got = b200.b200_w4g64_linear(
         x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
-        out_features=1536, in_features=8960, group_size=64, packing="canonical", algo=ALGOS["gemv"])
+        out_features=1536, in_features=8960, group_size=64, packing="canonical", algo=ALGOS[algo])
     assert got.dtype == dtype
     ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=1536, in_features=8960,
                      accumulate="f64")
-    assert_linear_close(got, ref, 1e-3, f"awq down {dtype} m={m}")
+    assert_linear_close(got, ref, 1e-3, f"awq down {dtype} m={m} {algo}")
 
 
 @pytest.mark.parametrize("bias_dtype", [torch.float16, torch.bfloat16, torch.float32])
@@ -284,3 +286,35 @@ def test_wrong_device_mix_is_rejected(b200, cuda_device):
         b200.b200_w4g64_linear(torch.zeros(1, 128, dtype=torch.bfloat16, device=cuda_device),
                                torch.from_numpy(qw), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
                                out_features=64, in_features=128, group_size=64, packing="canonical")
+
+
+@pytest.mark.parametrize("rows", [16, 32, 64, 128])
+@pytest.mark.parametrize("ksplit", [1, 2, 3, 5])
+def test_gemv_launch_shapes_agree(b200, cuda_device, rows, ksplit):
+    """Every forced launch shape (rows per CTA, cluster K split) gives the oracle's answer."""
+    from importlib import import_module
+
+    lib = import_module(b200.__name__ + "._lib").load()
+    k, n = 1536, 1000  # N not a multiple of any tile: exercises the ragged last CTA
+    qw, sc, z = _weights(k, n, "asym", 21)
+    x = torch.randn(5, k, generator=torch.Generator().manual_seed(22)).to(torch.bfloat16)
+    ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=n, in_features=k, accumulate="f64")
+    assert lib.qi4_gemv_mma_plan_override(rows, ksplit) == 0
+    try:
+        got = b200.b200_w4g64_linear(
+            x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
+            out_features=n, in_features=k, group_size=64, packing="canonical", algo=ALGOS["gemv"])
+    finally:
+        lib.qi4_gemv_mma_plan_override(0, 0)
+    assert_linear_close(got, ref, 1e-3, f"rows={rows} ksplit={ksplit}")
+
+
+def test_device_status_clean_after_kernels(b200, cuda_device):
+    from importlib import import_module
+
+    lib = import_module(b200.__name__ + "._lib").load()
+    qw, sc, z = _weights(1536, 256, "sym", 2)
+    x = torch.randn(1, 1536, device=cuda_device).to(torch.bfloat16)
+    b200.b200_w4g64_linear(x, to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
+                           out_features=256, in_features=1536, group_size=64, packing="canonical")
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
