@@ -298,7 +298,9 @@ int qi4_gemv_mma_plan_override(int rows, int ksplit) {
 
 int qi4_device_status(void* stream) {
   clear_error();
-  const int v = read_gemv_mma_error(static_cast<cudaStream_t>(stream));
+  const int v1 = read_gemv_mma_error(static_cast<cudaStream_t>(stream));
+  const int v2 = read_gemm_tc_error(static_cast<cudaStream_t>(stream));
+  const int v = (v1 < 0 || v2 < 0) ? -1 : (v1 | v2);
   if (v < 0) {
     set_error("cannot read the device error flags: %s", cudaGetErrorString(cudaGetLastError()));
     return QI4_ERR_LAUNCH;

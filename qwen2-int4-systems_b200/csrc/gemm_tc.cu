@@ -1,13 +1,489 @@
-// tcgen05 dequant-GEMM (prefill, M >= 128). Placeholder until the kernel lands.
+// Prefill dequant-GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// out[M, N] = x[M, K] @ deq(W)^T (+ bias), W4G64 canonical packing. Replaces
+// the fp32 `tl.dot` of _linear_canonical_w4g64_kernel (reference
+// src/qwen_int4/triton_kernels.py:66-116) for large M; numerics follow
+// torch_reference_linear (src/qwen_int4/backends.py:73-98) up to the bf16 (or
+// fp16) rounding of the dequantised weight fed to the tensor core.
+//
+// Tile: 128 weight rows (UMMA M) x BN tokens (UMMA N <= 256) x one 64-wide
+// group per pipeline stage, i.e. the product is computed as D^T = W x^T with
+// the dequantised weight as the 128-row A operand (dequant work per FLOP is
+// 1/BN) and the activations as the B operand; the FP32 accumulator lives in
+// TMEM (128 lanes x BN columns).
+//
+// Warp roles (10 warps):
+//   warp 0     TMA producer: packed-weight boxes [128 rows x 128 B] (4 groups)
+//              and activation tiles [BN rows x 64 elements], both with 128-byte
+//              swizzle, into shared-memory rings completing on mbarriers. The
+//              weight boxes are issued before griddepcontrol.wait.
+//   warp 1     allocates TMEM, then one lane issues 4 tcgen05.mma (K = 16 each)
+//              per stage and tcgen05.commit's the stage back to the producers.
+//   warps 2-9  dequantise: per stage each thread expands 32 codes of one row
+//              (exact FP32 w = (c - z) * s via the 1 + (c+8)/16 trick, one
+//              rounding to bf16/fp16) and stores them in the UMMA canonical
+//              K-major SW128 layout (16-byte chunk j of row r at j ^ (r % 8));
+//              then, after the last MMA, the same warps are the epilogue:
+//              tcgen05.ld 32 lanes x 32 columns, + bias (FP32), cast, store.
+// Every mbarrier wait is bounded (tma_util.cuh); no TMA multicast is used.
+#include <algorithm>
+#include <cstring>
+
 #include "gemm_tc.cuh"
+#include "qi4_common.cuh"
+#include "tma_util.cuh"
 
 namespace qi4 {
 
-bool tc_supported(int64_t, int64_t, int64_t, int) { return false; }
+__device__ int g_gemm_tc_error;
 
-cudaError_t launch_gemm_tc(const void*, int, int64_t, int64_t, const uint8_t*, const uint16_t*, const uint8_t*,
-                           const void*, int, void*, int64_t, cudaStream_t, bool, int) {
-  return cudaErrorNotSupported;
+namespace {
+
+constexpr int kStages = 3;      // A (dequantised) + B (activations) stages
+constexpr int kPStages = 2;     // packed-weight boxes (4 groups each)
+constexpr int kTileN = 128;     // weight rows per tile (UMMA M)
+constexpr int kDeqWarps = 16;
+constexpr int kThreads = 64 + 32 * kDeqWarps;  // producer + MMA + dequant/epilogue warps
+
+// Tensor-memory columns: the FP32 accumulator (BN) plus kStages A stages of 32
+// columns (64 bf16 K elements of 128 rows), rounded up to a power of two.
+__host__ __device__ constexpr uint32_t tmem_cols(int bn) {
+  return bn + 32 * 3 <= 128 ? 128u : (bn + 32 * 3 <= 256 ? 256u : 512u);
+}
+constexpr int kABytes = kTileN * 128;   // one group of 128 rows in bf16: 16 KB
+constexpr int kPBytes = kTileN * 128;   // one packed box: 128 rows x 128 B
+
+struct Args {
+  int M;
+  int64_t N, K;
+  const __half* scales;
+  const uint8_t* zeros;
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int out_dtype;
+  int BN;
+  int tma_out;  // 1: output tile staged in shared memory and written by one TMA store
+};
+
+// ---- tcgen05 wrappers ------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Same, with the A operand read from tensor memory (lane = row, 32-bit column =
+// two consecutive K elements).
+__device__ __forceinline__ void tc_mma_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 8 consecutive 32-bit columns from registers into tensor memory,
+// waiting until the writes have completed.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint4& a, const uint4& b) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr), "r"(a.x),
+      "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread completes.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), start address in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;             // leading-byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride-byte offset
+  d |= (uint64_t)1 << 46;             // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D = F32, A = B = bf16 (1) or f16 (0),
+// both K-major, N = bn, M = 128.
+__host__ __device__ constexpr uint32_t make_idesc(int ab_bf16, int bn) {
+  return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) | ((uint32_t)(bn >> 3) << 17) |
+         ((uint32_t)(kTileN >> 4) << 24);
+}
+
+// 8 codes (one packed word) -> 8 dequantised values packed as 4 x bf16x2/f16x2.
+template <int XT>
+__device__ __forceinline__ uint4 dequant_word(uint32_t word, float s16, float nz) {
+  uint32_t lo, hi;
+  expand_nibbles(word, lo, hi);
+  const float w0 = fmaf(nibble_float<0>(lo), s16, nz), w1 = fmaf(nibble_float<0>(hi), s16, nz);
+  const float w2 = fmaf(nibble_float<1>(lo), s16, nz), w3 = fmaf(nibble_float<1>(hi), s16, nz);
+  const float w4 = fmaf(nibble_float<2>(lo), s16, nz), w5 = fmaf(nibble_float<2>(hi), s16, nz);
+  const float w6 = fmaf(nibble_float<3>(lo), s16, nz), w7 = fmaf(nibble_float<3>(hi), s16, nz);
+  uint4 r;
+  if constexpr (XT == QI4_DTYPE_F16) {
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r.x) : "f"(w1), "f"(w0));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r.y) : "f"(w3), "f"(w2));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r.z) : "f"(w5), "f"(w4));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r.w) : "f"(w7), "f"(w6));
+  } else {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.x) : "f"(w1), "f"(w0));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.y) : "f"(w3), "f"(w2));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.z) : "f"(w5), "f"(w4));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r.w) : "f"(w7), "f"(w6));
+  }
+  return r;
+}
+
+template <int XT, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap omap, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kBBytes = BN * 128;                 // BN rows x 64 elements (2 bytes)
+  constexpr uint32_t kTmemCols = tmem_cols(BN);     // D (BN columns) + A stages (32 columns each)
+  uint8_t* sB = smem;                               // kStages x BN*128
+  uint8_t* sP = sB + kStages * kBBytes;             // kPStages x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPStages * kPBytes);
+  uint64_t* b_full = bars;                  // [kStages]   TMA(x) -> MMA
+  uint64_t* a_full = b_full + kStages;      // [kStages]   dequant -> MMA (kDeqWarps arrivals)
+  uint64_t* empty = a_full + kStages;       // [kStages]   MMA commit -> producers
+  uint64_t* p_full = empty + kStages;       // [kPStages]  TMA(packed) -> dequant
+  uint64_t* p_empty = p_full + kPStages;    // [kPStages]  dequant -> TMA(packed) (kDeqWarps arrivals)
+  uint64_t* acc_full = p_empty + kPStages;  // final commit -> epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t n0 = (int64_t)blockIdx.x * kTileN;
+  const int m0 = blockIdx.y * BN;
+  const int KT = (int)(a.K / kGroup);  // pipeline steps (one group each)
+
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&a_full[i], kDeqWarps);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&p_full[i], 1);
+      mbar_init(&p_empty[i], kDeqWarps);
+    }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;        // accumulator: columns [0, BN)
+  const uint32_t tmem_a = tmem_d + BN;       // A stages: columns [BN + 32 s, BN + 32 s + 32)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      prefetch_tensor_map(&wmap);
+      prefetch_tensor_map(&xmap);
+      const int nbox = (KT + 3) / 4;
+      // Weight boxes do not depend on the previous kernel: issue the first ones now.
+      int pbox = 0;
+      for (; pbox < kPStages && pbox < nbox; ++pbox) {
+        mbar_arrive_expect_tx(&p_full[pbox], kPBytes);
+        tma_load_2d(sP + pbox * kPBytes, &wmap, pbox * 128, (int)n0, &p_full[pbox]);
+      }
+      pdl_wait();
+      for (int k = 0; k < KT; ++k) {
+        const int s = k % kStages;
+        const uint32_t ph = (uint32_t)(k / kStages) & 1u;
+        mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
+        mbar_arrive_expect_tx(&b_full[s], kBBytes);
+        tma_load_2d(sB + s * kBBytes, &xmap, k * kGroup, m0, &b_full[s]);
+        if ((k & 3) == 3 && pbox < nbox) {  // refill the packed ring
+          const int p = pbox % kPStages;
+          const uint32_t pph = (uint32_t)(pbox / kPStages) & 1u;
+          mbar_wait(&p_empty[p], pph ^ 1u, &g_gemm_tc_error);
+          mbar_arrive_expect_tx(&p_full[p], kPBytes);
+          tma_load_2d(sP + p * kPBytes, &wmap, pbox * 128, (int)n0, &p_full[p]);
+          ++pbox;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = make_idesc(XT == QI4_DTYPE_F16 ? 0 : 1, BN);
+      for (int k = 0; k < KT; ++k) {
+        const int s = k % kStages;
+        const uint32_t ph = (uint32_t)(k / kStages) & 1u;
+        mbar_wait(&a_full[s], ph, &g_gemm_tc_error);
+        mbar_wait(&b_full[s], ph, &g_gemm_tc_error);
+        tc_fence_after();
+        const uint64_t bdesc = sw128_desc(smem_addr(sB + s * kBBytes));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // K = 16 per MMA: 8 TMEM columns of A, +32 bytes of B
+          tc_mma_ta(tmem_d, tmem_a + 32 * s + 8 * kk, bdesc + 2 * kk, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ---------------- dequantise (warps 2..17) into tensor memory ----------------
+    // A warp may only access the TMEM lanes of its quarter (warp % 4): warp w
+    // dequantises rows 32 (w % 4) + lane, codes 16 sub .. 16 sub + 15 of each
+    // group (sub = (w - 2) / 4), i.e. 8 packed bytes -> 8 TMEM columns.
+    const int quarter = warp & 3;
+    const int sub = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;  // tile row 0..127
+    const int64_t row = n0 + r;
+    const bool row_ok = row < a.N;
+    const int64_t G = a.K / kGroup;
+    const __half* srow = a.scales + (row_ok ? row : 0) * G;
+    const int64_t zrow = (row_ok ? row : 0) * G;
+    const uint32_t sP_addr = smem_addr(sP);
+    const uint32_t t_lane = (uint32_t)(quarter * 32) << 16;
+    const int nbox = (KT + 3) / 4;
+    // Scales / zero points of a whole box (4 groups) are prefetched one box ahead.
+    float sc4[4], nsc4[4];
+    int z4[4], nz4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sc4[j] = (row_ok && j < KT) ? __half2float(__ldg(srow + j)) : 0.f;
+      z4[j] = (row_ok && j < KT) ? load_zero(a.zeros, zrow + j) : 0;
+    }
+    for (int pb = 0; pb < nbox; ++pb) {
+      const int p = pb % kPStages;
+      const uint32_t pph = (uint32_t)(pb / kPStages) & 1u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kn = (pb + 1) * 4 + j;
+        nsc4[j] = (row_ok && kn < KT) ? __half2float(__ldg(srow + kn)) : 0.f;
+        nz4[j] = (row_ok && kn < KT) ? load_zero(a.zeros, zrow + kn) : 0;
+      }
+      mbar_wait(&p_full[p], pph, &g_gemm_tc_error);
+      uint2 q[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        q[j] = lds64(sP_addr + p * kPBytes + r * 128 + (((j * 2 + (sub >> 1)) ^ (r & 7)) << 4) + ((sub & 1) << 3));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_empty[p]);  // box consumed into registers
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int k = pb * 4 + j;
+        if (k >= KT) break;
+        const int s = k % kStages;
+        const uint32_t ph = (uint32_t)(k / kStages) & 1u;
+        const float s16 = 16.0f * sc4[j], nz = -static_cast<float>(24 + z4[j]) * sc4[j];
+        const uint4 d0 = dequant_word<XT>(q[j].x, s16, nz);
+        const uint4 d1 = dequant_word<XT>(q[j].y, s16, nz);
+        mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
+        tc_fence_after();
+        tmem_st8(tmem_a + t_lane + (uint32_t)(32 * s + 8 * sub), d0, d1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[s]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sc4[j] = nsc4[j];
+        z4[j] = nz4[j];
+      }
+    }
+
+    // ---------------- epilogue ----------------
+    mbar_wait(acc_full, 0, &g_gemm_tc_error);
+    tc_fence_after();
+    constexpr int kSlices = kDeqWarps / 4;                         // warps per lane quarter
+    constexpr int kCols = BN / kSlices >= 32 ? BN / kSlices : 32;  // columns per warp (TMEM loads are x32)
+    const int er = quarter * 32 + lane;                            // tile row of this thread
+    const int64_t orow = n0 + er;
+    const float bv = (orow < a.N && a.bias) ? load_as_f32(a.bias, a.bias_dtype, orow) : 0.f;
+    // Output tile staged as [BN tokens][128 rows] (256-byte rows) in the
+    // activation ring, which the finished main loop no longer uses.
+    uint16_t* sO = reinterpret_cast<uint16_t*>(sB);
+#pragma unroll 1
+    for (int c0 = sub * kCols; c0 < (sub + 1) * kCols && c0 < BN; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld32(tmem_d + t_lane + (uint32_t)c0, v);
+      if (a.tma_out) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float f = __uint_as_float(v[j]) + bv;
+          sO[(c0 + j) * kTileN + er] = a.out_dtype == QI4_DTYPE_F16 ? __half_as_ushort(__float2half_rn(f))
+                                                                   : __bfloat16_as_ushort(__float2bfloat16_rn(f));
+        }
+      } else if (orow < a.N) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = m0 + c0 + j;
+          if (m < a.M) store_from_f32(a.out, a.out_dtype, (int64_t)m * a.N + orow, __uint_as_float(v[j]) + bv);
+        }
+      }
+    }
+    if (a.tma_out) {
+      fence_proxy_async_smem();  // staged tile -> visible to the TMA engine
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * kDeqWarps) : "memory");  // the dequant/epilogue warps only
+      if (warp == 2 && lane == 0) {
+        tma_store_2d(&omap, (int)n0, m0, sO);
+        tma_store_commit_and_wait();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_d, kTmemCols);
+  }
+}
+
+size_t smem_bytes(int BN) {
+  return 1024 + (size_t)kStages * BN * 128 + (size_t)kPStages * kPBytes +
+         (3 * kStages + 2 * kPStages + 1) * sizeof(uint64_t) + 16;
+}
+
+template <int XT, int BN>
+cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const Args& a,
+                      cudaStream_t stream, bool pdl) {
+  auto kernel = gemm_tc_kernel<XT, BN>;
+  static unsigned long long configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(BN));
+    if (e != cudaSuccess) return e;
+    configured |= bit;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes(BN);
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, omap, a);
+}
+
+template <int XT>
+cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const Args& a,
+                     cudaStream_t s, bool pdl) {
+  switch (a.BN) {
+    case 64: return launch_bn<XT, 64>(wmap, xmap, omap, a, s, pdl);
+    case 128: return launch_bn<XT, 128>(wmap, xmap, omap, a, s, pdl);
+    default: return launch_bn<XT, 256>(wmap, xmap, omap, a, s, pdl);
+  }
+}
+
+}  // namespace
+
+bool tc_supported(int64_t M, int64_t N, int64_t K, int x_dtype) {
+  (void)N;
+  return M >= 1 && K >= kGroup && K % kGroup == 0 && (x_dtype == QI4_DTYPE_BF16 || x_dtype == QI4_DTYPE_F16);
+}
+
+cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                           const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
+                           int64_t N, cudaStream_t stream, bool pdl, int num_sms) {
+  Args a;
+  a.M = (int)M;
+  a.N = N;
+  a.K = K;
+  a.scales = reinterpret_cast<const __half*>(scales);
+  a.zeros = zeros;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.out = out;
+  a.out_dtype = x_dtype;
+  // Token-tile width: tiles per SM x per-tile cost, the per-tile cost being
+  // the MMA time (proportional to BN) plus a dequantisation share that does
+  // not shrink with BN.
+  {
+    const int64_t ntiles = (N + kTileN - 1) / kTileN;
+    double best = 1e30;
+    a.BN = 64;
+    for (int bn : {256, 128, 64}) {
+      if (bn > 64 && M <= bn / 2) continue;
+      const int64_t ctas = ntiles * ((M + bn - 1) / bn);
+      const double waves = (double)((ctas + num_sms - 1) / num_sms);
+      const double t = waves * (bn + 96.0);
+      if (t < best) {
+        best = t;
+        a.BN = bn;
+      }
+    }
+  }
+  CUtensorMap wmap, xmap;
+  if (!tensor_map_2d(&wmap, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
+                     (uint64_t)(K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (!tensor_map_2d(&xmap, x, x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                     (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  // Output tile by TMA store when the row pitch allows a tensor map (N * 2
+  // bytes a multiple of 16 and a 16-byte-aligned base); otherwise direct stores.
+  CUtensorMap omap;
+  memset(&omap, 0, sizeof(omap));
+  a.tma_out = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+              tensor_map_2d(&omap, out, x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                            (uint64_t)N, (uint64_t)M, (uint64_t)N * 2, kTileN, (uint32_t)a.BN,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+  return x_dtype == QI4_DTYPE_F16 ? launch_x<QI4_DTYPE_F16>(wmap, xmap, omap, a, stream, pdl)
+                                  : launch_x<QI4_DTYPE_BF16>(wmap, xmap, omap, a, stream, pdl);
+}
+
+int read_gemm_tc_error(cudaStream_t stream) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_gemm_tc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbolAsync(g_gemm_tc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
+  }
+  return v;
 }
 
 }  // namespace qi4

@@ -13,4 +13,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
                            int64_t N, cudaStream_t stream, bool pdl, int num_sms);
 
+// Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
+int read_gemm_tc_error(cudaStream_t stream);
+
 }  // namespace qi4

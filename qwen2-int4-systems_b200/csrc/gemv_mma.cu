@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
   const int r_lo = rb * 16 + gq;
   // Rows r and r + 8 share r % 8 (the swizzle phase): the lane's 8 bytes of
   // group g sit in 16-byte chunk (2 (g % 4) + tq / 2) XOR (r % 8), half tq % 2.
-  const uint8_t* a_row = wsm + r_lo * kBoxBytes + ((tq & 1) << 3);
+  const uint32_t a_row = smem_addr(wsm) + r_lo * kBoxBytes + ((tq & 1) << 3);
   const TableEntry* t_lo = table + r_lo * tstride;
   const TableEntry* t_hi = t_lo + 8 * tstride;
 
@@ -305,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
       const int g = gbat + j;
       if (g >= ge) break;
       const int chunk = ((((g & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4;
-      const uint8_t* ap = a_row + (size_t)(g >> 2) * R * kBoxBytes + chunk;
-      const uint2 wl = *reinterpret_cast<const uint2*>(ap);
-      const uint2 wh = *reinterpret_cast<const uint2*>(ap + 8 * kBoxBytes);
+      const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes + chunk);
+      const uint2 wl = lds64(ap);
+      const uint2 wh = lds64(ap + 8 * kBoxBytes);
       const TableEntry el = t_lo[g], eh = t_hi[g];
       uint32_t al[8], ah[8];
       expand_word<XT>(wl.x, el.zc2, al);
