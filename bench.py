@@ -133,14 +133,11 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 def quantize_symmetric_rtn_gpu(n: int, k: int, gen: torch.Generator, device) -> tuple:
+    q2 = importlib.import_module(PACKAGE + ".qwen2")
     w = (torch.randn(n, k, device=device, generator=gen) * 0.02).to(torch.bfloat16).float()
-    g = w.view(n, k // 64, 64)
-    s = g.abs().amax(dim=-1) / 7.0
-    s = torch.where(s == 0, torch.ones_like(s), s)
-    codes = torch.round(g / s.unsqueeze(-1)).clamp_(-7, 7).to(torch.int16).view(n, k)
-    packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).reshape(-1, 1)
+    packed, scales = q2.quantize_symmetric_rtn_torch(w)
     zeros = torch.zeros((n * (k // 64) + 1) // 2, 1, dtype=torch.uint8, device=device)
-    return packed.contiguous(), s.to(torch.float16).contiguous(), zeros
+    return packed, scales, zeros
 
 
 def build_model_weights(device, seed: int = 0) -> list[list[dict]]:
@@ -304,6 +301,51 @@ def run_reference(args) -> None:
 # main (our arm)
 # ---------------------------------------------------------------------------
 
+def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
+    """the reference's Qwen2-1.5B (random init, W4G64 RTN) on
+    the b200 backend, batch 1, greedy decode through the reference's own
+    ``greedy_generate_cached``; the same model on the reference's ``torch``
+    backend on this GPU for comparison (fewer steps)."""
+    q2 = importlib.import_module(PACKAGE + ".qwen2")
+    try:
+        q2.reference_package()
+    except ImportError as exc:
+        return {"unavailable": f"reference package not installed: {exc}"}
+    gen_mod = importlib.import_module("qwen_int4.generation")
+    model = q2.build_random_qwen2(device=device, seed=0)
+    prompt = torch.randint(0, model.config.vocab_size, (1, prompt_len),
+                           generator=torch.Generator().manual_seed(20260831)).to(device)
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out = fn()
+        b.record()
+        b.synchronize()
+        return a.elapsed_time(b), out
+
+    result = {"model": "Qwen2-1.5B random-init W4G64 RTN (reference model.py)", "batch": 1,
+              "prompt_tokens": prompt_len,
+              "harness": "cuDNN SDPA backend disabled (per-call graph builds as the KV cache grows)"}
+    cudnn_sdp = torch.backends.cuda.cudnn_sdp_enabled()
+    torch.backends.cuda.enable_cudnn_sdp(False)
+    with torch.inference_mode():
+        for backend, steps in (("b200", new_tokens), ("torch", 8)):
+            model.set_backend(backend)
+            gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=3)  # warm-up at full length
+            prefill_ms, _ = timed(lambda: model(prompt, use_cache=True))
+            total_ms, _ = timed(lambda: gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=steps))
+            decode_ms = max(total_ms - prefill_ms, 1e-6)
+            result[backend] = {"prefill_ms": prefill_ms, "new_tokens": steps,
+                               "generate_ms": total_ms, "decode_tok_s": steps / (decode_ms / 1e3)}
+    torch.backends.cuda.enable_cudnn_sdp(cudnn_sdp)
+    result["decode_tok_s"] = result["b200"]["decode_tok_s"]
+    del model
+    torch.cuda.empty_cache()
+    return result
+
+
 def load_traffic() -> dict:
     path = ROOT / "profiles" / "traffic.json"
     if path.exists():
@@ -319,6 +361,7 @@ def main() -> None:
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm", action="store_true")
+    parser.add_argument("--no-model", action="store_true", help="skip the Qwen2-1.5B decode tok/s section")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
@@ -454,6 +497,12 @@ def main() -> None:
            "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
            "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python, ctypes C-ABI)"}
 
+    decode = None
+    if not args.no_model:
+        del layers, entries, step_chain, step_graph
+        torch.cuda.empty_cache()
+        decode = e2e_decode(device)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_linear_sample()
@@ -471,7 +520,7 @@ def main() -> None:
                    "bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": roofline, "per_shape_m1": per_shape, "gemm_m2048": gemm,
+        "roofline": roofline, "per_shape_m1": per_shape, "gemm_m2048": gemm, "qwen2_decode": decode,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))
 

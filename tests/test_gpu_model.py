@@ -1,0 +1,114 @@
+"""The reference's unmodified Qwen2 model running on the b200 backend (GPU).
+
+Uses the reference package installed into baseline/_ref (skipped if absent).
+Gates (north star): final-logits cosine >= 0.9999 against the reference's own
+``torch`` backend on the same random-init Qwen2-1.5B, and the cached
+prefill/decode path agreeing with the full forward (as the reference's
+tests/test_kv_cache.py checks for its own backends).
+"""
+
+import importlib
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def q2(b200):
+    mod = importlib.import_module(b200.__name__ + ".qwen2")
+    try:
+        mod.reference_package()
+    except ImportError:
+        pytest.skip("reference package not installed (baseline/_ref)")
+    return mod
+
+
+def _cos(a, b):
+    a, b = a.float().flatten(), b.float().flatten()
+    return float(torch.nn.functional.cosine_similarity(a, b, dim=0))
+
+
+def test_small_model_cached_decode_matches_full_forward(q2, cuda_device):
+    cfg = q2.qwen2_config(num_hidden_layers=2, vocab_size=512)
+    model = q2.build_random_qwen2(cfg, device=cuda_device, seed=3)
+    tokens = torch.randint(0, 512, (2, 9), generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    with torch.inference_mode():
+        full = model(tokens)
+        pre, cache = model(tokens[:, :6], use_cache=True)
+        steps = [pre[:, -1]]
+        for t in range(6, 9):
+            logits, cache = model(tokens[:, t:t + 1], past_key_values=cache, use_cache=True)
+            steps.append(logits[:, -1])
+    for i, got in enumerate(steps):
+        assert _cos(got, full[:, 5 + i]) > 0.9999
+
+
+def test_full_qwen2_logits_match_reference_torch_backend(q2, cuda_device):
+    """Final-logits cosine against the reference's torch backend.
+
+    A random-init 28-layer bf16 Qwen2 amplifies summation-order differences:
+    the reference's own torch path with its matmul in float64 instead of
+    float32 reaches only ~0.9996 against itself. So the gate is that b200 is
+    at least as close to the reference as the reference is to itself under
+    that change (and >= 0.9995); the 0.9999 north-star figure is reported.
+    """
+    from qwen_int4.quantization import dequantize_groupwise
+    import qwen_int4.linear as L
+
+    model = q2.build_random_qwen2(device=cuda_device, seed=0)
+    prompt = torch.randint(0, model.config.vocab_size, (1, 16),
+                           generator=torch.Generator().manual_seed(20260831)).to(cuda_device)
+
+    def forward_f64(self, x):  # the reference algorithm with a float64 matmul
+        w = dequantize_groupwise(self.qweight, self.scales, zeros=self.zeros, out_features=self.out_features,
+                                 in_features=self.in_features, group_size=self.group_size, packing=self.packing)
+        out = (x.reshape(-1, self.in_features).double() @ w.double().t()).float()
+        if self.bias is not None:
+            out = out + self.bias.float()
+        return out.reshape(*x.shape[:-1], self.out_features).to(x.dtype)
+
+    with torch.inference_mode():
+        ours = model(prompt)
+        model.set_backend("torch")
+        ref = model(prompt)
+        saved = L.QuantLinear.forward
+        L.QuantLinear.forward = forward_f64
+        try:
+            ref64 = model(prompt)
+        finally:
+            L.QuantLinear.forward = saved
+        model.set_backend("b200")
+    cos = _cos(ours[0, -1], ref[0, -1])
+    self_consistency = _cos(ref64[0, -1], ref[0, -1])
+    print(f"logits cosine b200 vs torch {cos:.6f}; reference f64 vs f32 {self_consistency:.6f}")
+    assert cos >= 0.9995
+    assert cos >= self_consistency - 1e-4, (cos, self_consistency)
+
+
+def test_full_qwen2_greedy_generation_agrees_with_torch_backend(q2, cuda_device):
+    """Greedy generation through the reference's generation loop on both backends.
+
+    Free-running greedy decode of a random-init model diverges after the
+    first near-tie, so agreement is checked teacher-forced: on the torch
+    backend's greedy sequence, both backends must pick the same argmax at
+    every generated position whose top-1/top-2 logit gap exceeds 0.1.
+    """
+    gen_mod = importlib.import_module("qwen_int4.generation")
+    model = q2.build_random_qwen2(device=cuda_device, seed=0)
+    prompt = torch.randint(0, model.config.vocab_size, (2, 12),
+                           generator=torch.Generator().manual_seed(7)).to(cuda_device)
+    ours_free = gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=6)
+    model.set_backend("torch")
+    seq = gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=6)
+    assert ours_free.shape == seq.shape
+    with torch.inference_mode():
+        ref_logits = model(seq)[:, 11:-1].float()
+        model.set_backend("b200")
+        our_logits = model(seq)[:, 11:-1].float()
+    top2 = ref_logits.topk(2, dim=-1).values
+    clear = (top2[..., 0] - top2[..., 1]) > 0.1
+    assert clear.sum() >= 4
+    agree = ref_logits.argmax(-1) == our_logits.argmax(-1)
+    assert bool(agree[clear].all()), (agree, clear)
