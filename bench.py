@@ -346,6 +346,39 @@ def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
     return result
 
 
+def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> dict:
+    """one Qwen2-1.5B MLP (gate/up/down) at M tokens with
+    gate/up/down column-split over the ranks and NCCL all-gathers (two per
+    MLP). Time is the max over ranks of CUDA-event time per forward."""
+    par = importlib.import_module(PACKAGE + ".parallel")
+    from types import SimpleNamespace
+
+    gen = torch.Generator(device=device).manual_seed(5)
+
+    def qlinear(n, k):
+        qw, sc, z = quantize_symmetric_rtn_gpu(n, k, gen, device)
+        return SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=k, out_features=n)
+
+    mlp = SimpleNamespace(gate_proj=qlinear(8960, 1536), up_proj=qlinear(8960, 1536), down_proj=qlinear(1536, 8960))
+    split = par.ColumnParallelMLP(mlp)
+    x = torch.randn(m, 1536, device=device, generator=gen).to(torch.bfloat16)
+    for _ in range(3):
+        split(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        split(x)
+    b.record()
+    b.synchronize()
+    ms = torch.tensor([a.elapsed_time(b) / reps], device=device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    flops = 2 * m * 1536 * 8960 * 3
+    return {"m": m, "ms_per_mlp": float(ms.item()), "TFLOPs": flops / (float(ms.item()) / 1e3) / 1e12,
+            "collectives": "2 x all_gather_into_tensor (NCCL) per MLP", "ranks": world}
+
+
 def load_traffic() -> dict:
     path = ROOT / "profiles" / "traffic.json"
     if path.exists():
@@ -442,7 +475,7 @@ def main() -> None:
 
     # GEMM at M=2048 (tensor-core kernel) over one layer's seven shapes.
     gemm = None
-    if not args.no_gemm:
+    if not args.no_gemm and world == 1:
         gemm = {"m": 2048, "per_shape": {}}
         total_flops, total_ms = 0, 0.0
         for idx, (name, k, n, has_bias) in enumerate(SHAPES):
@@ -497,8 +530,10 @@ def main() -> None:
            "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
            "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python, ctypes C-ABI)"}
 
+    split = split_prefill(device, dist, world) if dist else None
+
     decode = None
-    if not args.no_model:
+    if not args.no_model and world == 1:
         del layers, entries, step_chain, step_graph
         torch.cuda.empty_cache()
         decode = e2e_decode(device)
@@ -521,6 +556,7 @@ def main() -> None:
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline, "per_shape_m1": per_shape, "gemm_m2048": gemm, "qwen2_decode": decode,
+        "split_prefill_mlp": split,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))
 

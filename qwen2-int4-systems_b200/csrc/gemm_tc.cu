@@ -173,10 +173,13 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t word, float s16, float nz
 template <int XT, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                   const __grid_constant__ CUtensorMap omap, const Args a) {
+                   const __grid_constant__ CUtensorMap xmap_lo, const __grid_constant__ CUtensorMap omap,
+                   const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kBBytes = BN * 128;                 // BN rows x 64 elements (2 bytes)
+  // FP32 activations arrive as two bf16 tiles (x = hi + lo), loaded together.
+  constexpr int kXTiles = XT == QI4_DTYPE_F32 ? 2 : 1;
+  constexpr int kBBytes = kXTiles * BN * 128;       // BN rows x 64 elements (2 bytes), per tile
   constexpr uint32_t kTmemCols = tmem_cols(BN);     // D (BN columns) + A stages (32 columns each)
   uint8_t* sB = smem;                               // kStages x BN*128
   uint8_t* sP = sB + kStages * kBBytes;             // kPStages x 16 KB
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer ----------------
       prefetch_tensor_map(&wmap);
       prefetch_tensor_map(&xmap);
+      if constexpr (kXTiles == 2) prefetch_tensor_map(&xmap_lo);
       const int nbox = (KT + 3) / 4;
       // Weight boxes do not depend on the previous kernel: issue the first ones now.
       int pbox = 0;
@@ -234,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
         mbar_arrive_expect_tx(&b_full[s], kBBytes);
         tma_load_2d(sB + s * kBBytes, &xmap, k * kGroup, m0, &b_full[s]);
+        if constexpr (kXTiles == 2) tma_load_2d(sB + s * kBBytes + BN * 128, &xmap_lo, k * kGroup, m0, &b_full[s]);
         if ((k & 3) == 3 && pbox < nbox) {  // refill the packed ring
           const int p = pbox % kPStages;
           const uint32_t pph = (uint32_t)(pbox / kPStages) & 1u;
@@ -247,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = make_idesc(XT == QI4_DTYPE_F16 ? 0 : 1, BN);
+      constexpr uint32_t idesc = make_idesc(XT == QI4_DTYPE_F16 ? 0 : 1, BN);  // FP32 x: bf16 hi/lo
       for (int k = 0; k < KT; ++k) {
         const int s = k % kStages;
         const uint32_t ph = (uint32_t)(k / kStages) & 1u;
@@ -258,6 +263,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)  // K = 16 per MMA: 8 TMEM columns of A, +32 bytes of B
           tc_mma_ta(tmem_d, tmem_a + 32 * s + 8 * kk, bdesc + 2 * kk, idesc, (k > 0 || kk > 0) ? 1u : 0u);
+        if constexpr (kXTiles == 2) {  // + W x_lo: the low bf16 half of FP32 activations
+          const uint64_t ldesc = sw128_desc(smem_addr(sB + s * kBBytes + BN * 128));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) tc_mma_ta(tmem_d, tmem_a + 32 * s + 8 * kk, ldesc + 2 * kk, idesc, 1u);
+        }
         tc_commit(&empty[s]);
       }
       tc_commit(acc_full);
@@ -333,9 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int er = quarter * 32 + lane;                            // tile row of this thread
     const int64_t orow = n0 + er;
     const float bv = (orow < a.N && a.bias) ? load_as_f32(a.bias, a.bias_dtype, orow) : 0.f;
-    // Output tile staged as [BN tokens][128 rows] (256-byte rows) in the
-    // activation ring, which the finished main loop no longer uses.
+    // Output tile staged as [BN tokens][128 rows] in the activation ring,
+    // which the finished main loop no longer uses.
     uint16_t* sO = reinterpret_cast<uint16_t*>(sB);
+    float* sO32 = reinterpret_cast<float*>(sB);
 #pragma unroll 1
     for (int c0 = sub * kCols; c0 < (sub + 1) * kCols && c0 < BN; c0 += 32) {
       uint32_t v[32];
@@ -344,8 +355,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float f = __uint_as_float(v[j]) + bv;
-          sO[(c0 + j) * kTileN + er] = a.out_dtype == QI4_DTYPE_F16 ? __half_as_ushort(__float2half_rn(f))
-                                                                   : __bfloat16_as_ushort(__float2bfloat16_rn(f));
+          if constexpr (XT == QI4_DTYPE_F32)
+            sO32[(c0 + j) * kTileN + er] = f;
+          else
+            sO[(c0 + j) * kTileN + er] = XT == QI4_DTYPE_F16 ? __half_as_ushort(__float2half_rn(f))
+                                                             : __bfloat16_as_ushort(__float2bfloat16_rn(f));
         }
       } else if (orow < a.N) {
 #pragma unroll
@@ -359,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();  // staged tile -> visible to the TMA engine
       asm volatile("bar.sync 1, %0;" ::"r"(32 * kDeqWarps) : "memory");  // the dequant/epilogue warps only
       if (warp == 2 && lane == 0) {
-        tma_store_2d(&omap, (int)n0, m0, sO);
+        tma_store_2d(&omap, (int)n0, m0, sB);
         tma_store_commit_and_wait();
       }
     }
@@ -374,44 +388,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-size_t smem_bytes(int BN) {
-  return 1024 + (size_t)kStages * BN * 128 + (size_t)kPStages * kPBytes +
+size_t smem_bytes(int BN, int x_tiles) {
+  return 1024 + (size_t)kStages * x_tiles * BN * 128 + (size_t)kPStages * kPBytes +
          (3 * kStages + 2 * kPStages + 1) * sizeof(uint64_t) + 16;
 }
 
 template <int XT, int BN>
-cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const Args& a,
-                      cudaStream_t stream, bool pdl) {
+cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
+                      const CUtensorMap& omap, const Args& a, cudaStream_t stream, bool pdl) {
+  const size_t smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1);
   auto kernel = gemm_tc_kernel<XT, BN>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes(BN));
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured |= bit;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes(BN);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[1];
   attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, omap, a);
+  return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, xmap_lo, omap, a);
 }
 
 template <int XT>
-cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& omap, const Args& a,
-                     cudaStream_t s, bool pdl) {
+cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
+                     const CUtensorMap& omap, const Args& a, cudaStream_t s, bool pdl) {
   switch (a.BN) {
-    case 64: return launch_bn<XT, 64>(wmap, xmap, omap, a, s, pdl);
-    case 128: return launch_bn<XT, 128>(wmap, xmap, omap, a, s, pdl);
-    default: return launch_bn<XT, 256>(wmap, xmap, omap, a, s, pdl);
+    case 64: return launch_bn<XT, 64>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 128: return launch_bn<XT, 128>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    default:
+      if constexpr (XT == QI4_DTYPE_F32) return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
+      else return launch_bn<XT, 256>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+  }
+}
+
+// FP32 activations -> two bf16 arrays with x = hi + lo (hi = bf16(x),
+// lo = bf16(x - hi)): 16 significant bits, the rest below 2^-17 |x|.
+__global__ void __launch_bounds__(256) split_f32_kernel(const float4* __restrict__ x, uint2* __restrict__ hi,
+                                                        uint2* __restrict__ lo, int64_t n4) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = __ldg(x + i);
+    uint32_t h0, h1, l0, l1;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h0) : "f"(v.y), "f"(v.x));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h1) : "f"(v.w), "f"(v.z));
+    const float r0 = v.x - __uint_as_float(h0 << 16), r1 = v.y - __uint_as_float(h0 & 0xFFFF0000u);
+    const float r2 = v.z - __uint_as_float(h1 << 16), r3 = v.w - __uint_as_float(h1 & 0xFFFF0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l0) : "f"(r1), "f"(r0));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l1) : "f"(r3), "f"(r2));
+    hi[i] = make_uint2(h0, h1);
+    lo[i] = make_uint2(l0, l1);
   }
 }
 
@@ -419,7 +454,8 @@ cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUt
 
 bool tc_supported(int64_t M, int64_t N, int64_t K, int x_dtype) {
   (void)N;
-  return M >= 1 && K >= kGroup && K % kGroup == 0 && (x_dtype == QI4_DTYPE_BF16 || x_dtype == QI4_DTYPE_F16);
+  return M >= 1 && K >= kGroup && K % kGroup == 0 &&
+         (x_dtype == QI4_DTYPE_BF16 || x_dtype == QI4_DTYPE_F16 || x_dtype == QI4_DTYPE_F32);
 }
 
 cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
@@ -444,6 +480,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
     a.BN = 64;
     for (int bn : {256, 128, 64}) {
       if (bn > 64 && M <= bn / 2) continue;
+      if (bn > 128 && x_dtype == QI4_DTYPE_F32) continue;  // two activation tiles per stage
       const int64_t ctas = ntiles * ((M + bn - 1) / bn);
       const double waves = (double)((ctas + num_sms - 1) / num_sms);
       const double t = waves * (bn + 96.0);
@@ -453,24 +490,52 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
       }
     }
   }
-  CUtensorMap wmap, xmap;
+  CUtensorMap wmap, xmap, xmap_lo, omap;
+  memset(&xmap_lo, 0, sizeof(xmap_lo));
+  memset(&omap, 0, sizeof(omap));
   if (!tensor_map_2d(&wmap, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
                      (uint64_t)(K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  if (!tensor_map_2d(&xmap, x, x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                     (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
-  // Output tile by TMA store when the row pitch allows a tensor map (N * 2
-  // bytes a multiple of 16 and a 16-byte-aligned base); otherwise direct stores.
-  CUtensorMap omap;
-  memset(&omap, 0, sizeof(omap));
-  a.tma_out = (N % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
-              tensor_map_2d(&omap, out, x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                            (uint64_t)N, (uint64_t)M, (uint64_t)N * 2, kTileN, (uint32_t)a.BN,
-                            CU_TENSOR_MAP_SWIZZLE_NONE);
-  return x_dtype == QI4_DTYPE_F16 ? launch_x<QI4_DTYPE_F16>(wmap, xmap, omap, a, stream, pdl)
-                                  : launch_x<QI4_DTYPE_BF16>(wmap, xmap, omap, a, stream, pdl);
+  // FP32 activations: split into bf16 hi / lo arrays in stream-ordered scratch.
+  void* scratch = nullptr;
+  const void* x_hi = x;
+  const void* x_lo = nullptr;
+  if (x_dtype == QI4_DTYPE_F32) {
+    const size_t half_bytes = (size_t)M * (size_t)K * 2;
+    cudaError_t e = cudaMallocAsync(&scratch, 2 * half_bytes, stream);
+    if (e != cudaSuccess) return e;
+    const int64_t n4 = M * K / 4;
+    const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms * 8);
+    split_f32_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float4*>(x), static_cast<uint2*>(scratch),
+                                                  reinterpret_cast<uint2*>(static_cast<char*>(scratch) + half_bytes),
+                                                  n4);
+    x_hi = scratch;
+    x_lo = static_cast<char*>(scratch) + half_bytes;
+  }
+  const CUtensorMapDataType xt = x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  bool ok = tensor_map_2d(&xmap, x_hi, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (ok && x_lo)
+    ok = tensor_map_2d(&xmap_lo, x_lo, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  cudaError_t e = cudaErrorInvalidValue;
+  if (ok) {
+    // Output tile by TMA store when the row pitch allows a tensor map (a
+    // multiple of 16 bytes, 16-byte-aligned base); otherwise direct stores.
+    const int osz = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
+    a.tma_out = ((N * osz) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+                tensor_map_2d(&omap, out,
+                              x_dtype == QI4_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                              : x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                              (uint64_t)N, (uint64_t)M, (uint64_t)N * osz, kTileN, (uint32_t)a.BN,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+    e = x_dtype == QI4_DTYPE_F16   ? launch_x<QI4_DTYPE_F16>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
+        : x_dtype == QI4_DTYPE_F32 ? launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
+                                   : launch_x<QI4_DTYPE_BF16>(wmap, xmap, xmap_lo, omap, a, stream, pdl);
+  }
+  if (scratch) cudaFreeAsync(scratch, stream);
+  return e;
 }
 
 int read_gemm_tc_error(cudaStream_t stream) {

@@ -85,8 +85,6 @@ def test_tc_ragged_shapes(b200, cuda_device, dtype, m, n, k):
 @pytest.mark.parametrize("key", G.LINEAR_CASES)
 def test_tc_on_reference_golden_cases(b200, cuda_device, key):
     c = G.linear_case(key)
-    if c["dtype"] == "f32":
-        pytest.skip("FP32 activations use the GEMV kernels (the tensor-core path takes bf16/fp16)")
     x = c["x"]
     got = b200.b200_w4g64_linear(
         x.to(cuda_device), to_dev(c["qweight"], cuda_device), to_dev(c["scales"], cuda_device),
@@ -110,8 +108,15 @@ def test_auto_dispatch_uses_tc_for_large_m_and_status_is_clean(b200, cuda_device
     assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
 
 
-def test_tc_rejects_fp32_activations_when_forced(b200, cuda_device):
-    qw, sc, z = _weights(128, 64, "sym", 5)
-    x = torch.randn(32, 128)
-    with pytest.raises(ValueError, match="tensor-core"):
-        _run(b200, cuda_device, x, qw, sc, z, None, 64, 128)
+@pytest.mark.parametrize(("m", "n", "k"), [(17, 256, 1536), (200, 1000, 192), (512, 1536, 8960)])
+def test_tc_fp32_activations_down_proj_path(b200, cuda_device, m, n, k):
+    """FP32 activations (the model's down_proj input) on the tensor-core path.
+
+    x is split into bf16 hi + lo (16 significant bits) and both halves go
+    through the MMA; the output is FP32 like the reference's for FP32 input.
+    """
+    qw, sc, z = _weights(k, n, "asym", 61)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(m + k)) * 0.5
+    got = _run(b200, cuda_device, x, qw, sc, z, None, n, k)
+    assert got.dtype == torch.float32
+    assert_linear_close(got, _ref(x, qw, sc, z, None, n, k), 2e-2, f"tc fp32 {m}x{n}x{k}")
