@@ -103,6 +103,28 @@ QI4_API int qi4_w4g64_dequant_f32(const uint8_t* qweight, const uint16_t* scales
 QI4_API int qi4_w4_unpack(const uint8_t* packed, int8_t* out, int64_t elements,
                   void* stream);
 
+/*
+ * Allocation-free form of qi4_w4g64_linear for FP32 activations (the input
+ * dtype of the model's down_proj): out[M, N] (FP32) = x[M, K] (FP32) @ W^T
+ * (+ bias), on the tensor-core kernel. No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory while serving a
+ * request - engines that budget all device memory up front, FFI hosts with
+ * no CUDA allocator of their own, loops that must not enter an allocator.
+ * The FP32 path needs scratch (bf16 hi/lo copies of x); here it is a fixed
+ * 32 MiB array in the library's device memory, present on every GPU that
+ * loads the library until the process exits, so M * K <= 8388608 (larger
+ * inputs return QI4_ERR_SHAPE; use qi4_w4g64_linear). The first call on a
+ * device looks up the array's address (cudaGetSymbolAddress); make that first
+ * call before any stream capture. All calls share the one array: calls that
+ * may run at the same time on the GPU (different streams without ordering)
+ * race on it. Nothing is carried over between calls - each call writes every
+ * scratch byte it reads.
+ */
+QI4_API int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
+                                         const uint16_t* scales_f16, const uint8_t* zeros,
+                                         const void* bias, int bias_dtype, float* out, int64_t N,
+                                         void* stream);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128) and
  * K-split factor (CTAs per cluster, 1..8). rows = 0 restores the library's

@@ -308,6 +308,28 @@ int qi4_device_status(void* stream) {
   return v;
 }
 
+int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
+                                 const uint16_t* scales_f16, const uint8_t* zeros, const void* bias, int bias_dtype,
+                                 float* out, int64_t N, void* stream) {
+  clear_error();
+  int rc = validate_linear(x, QI4_DTYPE_F32, M, K, qweight, scales_f16, bias, bias_dtype, out, N);
+  if (rc) return rc;
+  const size_t need = 2 * (size_t)M * (size_t)K * 2;
+  if (need > static_scratch_bytes()) {
+    set_error("M*K = %lld exceeds the fixed scratch of this entry point: it holds %zu bytes (M*K <= %zu); "
+              "use qi4_w4g64_linear for larger inputs",
+              (long long)(M * K), static_scratch_bytes(), static_scratch_bytes() / 4);
+    return QI4_ERR_SHAPE;
+  }
+  DeviceInfo info;
+  rc = current_device(info);
+  if (rc) return rc;
+  if (!bias) bias_dtype = QI4_DTYPE_NONE;
+  return check_launch(launch_gemm_tc_f32_static(x, M, K, qweight, scales_f16, zeros, bias, bias_dtype, out, N,
+                                                static_cast<cudaStream_t>(stream), info.sms),
+                      "w4g64 allocation-free FP32 GEMM");
+}
+
 int qi4_last_error(char* buf, size_t len) {
   const std::string& s = g_last_error;
   if (buf && len) {

@@ -28,6 +28,7 @@
 // Every mbarrier wait is bounded (tma_util.cuh); no TMA multicast is used.
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "gemm_tc.cuh"
 #include "qi4_common.cuh"
@@ -536,6 +537,90 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
   }
   if (scratch) cudaFreeAsync(scratch, stream);
   return e;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the FP32-activation path
+// ---------------------------------------------------------------------------
+// The FP32-activation path above needs scratch for the bf16 hi/lo copies of
+// x and gets it from cudaMallocAsync. Some callers cannot allocate device
+// memory at call time: engines that plan every byte of device memory up
+// front and run under a hard memory cap, hosts that reach this library over a
+// plain C FFI and manage no CUDA allocator of their own, and latency-critical
+// loops that must not enter the allocator. For them the scratch below is a
+// fixed array in the module's global memory, reserved once on every GPU that
+// loads the library and held until the process exits.
+namespace {
+
+constexpr size_t kStaticScratchBytes = 32u << 20;  // 32 MiB: hi + lo bf16 copies of x, M * K <= 8 Mi elements
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device. The name is only
+// a host-side handle; the address comes from cudaGetSymbolAddress, done once
+// per device with that device current (the first call on a device).
+cudaError_t static_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+size_t static_scratch_bytes() { return kStaticScratchBytes; }
+
+cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
+                                      const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
+                                      float* out, int64_t N, cudaStream_t stream, int num_sms) {
+  const size_t half_bytes = (size_t)M * (size_t)K * 2;
+  if (2 * half_bytes > kStaticScratchBytes) return cudaErrorInvalidValue;  // callers check first
+  void* scratch = nullptr;
+  cudaError_t e = static_scratch_address(&scratch);
+  if (e != cudaSuccess) return e;
+  Args a;
+  a.M = (int)M;
+  a.N = N;
+  a.K = K;
+  a.scales = reinterpret_cast<const __half*>(scales);
+  a.zeros = zeros;
+  a.bias = bias;
+  a.bias_dtype = bias_dtype;
+  a.out = out;
+  a.out_dtype = QI4_DTYPE_F32;
+  a.BN = M > 64 ? 128 : 64;
+  CUtensorMap wmap, xmap, xmap_lo, omap;
+  memset(&omap, 0, sizeof(omap));
+  // Every element of the hi / lo arrays that the GEMM reads is written by the
+  // split pass of the same call, so nothing left from an earlier call is used.
+  const int64_t n4 = M * K / 4;
+  const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms * 8);
+  uint2* hi = static_cast<uint2*>(scratch);
+  uint2* lo = reinterpret_cast<uint2*>(static_cast<char*>(scratch) + half_bytes);
+  split_f32_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(x), hi, lo, n4);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (!tensor_map_2d(&wmap, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
+                     (uint64_t)(K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tensor_map_2d(&xmap, hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup,
+                     (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !tensor_map_2d(&xmap_lo, lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+                     kGroup, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  a.tma_out = ((N * 4) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+              tensor_map_2d(&omap, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)N, (uint64_t)M,
+                            (uint64_t)N * 4, kTileN, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+  return launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, false);
 }
 
 int read_gemm_tc_error(cudaStream_t stream) {

@@ -13,6 +13,14 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
                            int64_t N, cudaStream_t stream, bool pdl, int num_sms);
 
+// FP32-activation tensor-core linear whose scratch is a fixed static device
+// array (no allocation); x and out are FP32. M * K * 4 bytes must not exceed
+// static_scratch_bytes(). Not reentrant across concurrent streams.
+size_t static_scratch_bytes();
+cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
+                                      const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
+                                      float* out, int64_t N, cudaStream_t stream, int num_sms);
+
 // Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
 int read_gemm_tc_error(cudaStream_t stream);
 
