@@ -379,6 +379,23 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
             "collectives": "2 x all_gather_into_tensor (NCCL) per MLP", "ranks": world}
 
 
+def profile_case(kind: str) -> None:
+    """Small, ncu-sized run of the dominant kernel (see --profile-case)."""
+    device = torch.device("cuda", 0)
+    lib = importlib.import_module(PACKAGE + "._lib").load()
+    gen = torch.Generator(device=device).manual_seed(0)
+    ents = []
+    for _ in range(8):
+        qw, sc, z = quantize_symmetric_rtn_gpu(8960, 1536, gen, device)
+        ents.append({"name": "gate", "k": 1536, "n": 8960, "qweight": qw, "scales": sc, "zeros": z, "bias": None})
+    m, algo = (1, 1) if kind == "gemv" else (2048, 2)
+    chain = Chain(lib, ents if kind == "gemv" else ents[:2], m, device, gen, algo=algo)
+    for _ in range(3):
+        chain.launch()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": kind, "launches": 3 * len(chain.entries), "m": m}))
+
+
 def load_traffic() -> dict:
     path = ROOT / "profiles" / "traffic.json"
     if path.exists():
@@ -395,11 +412,17 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm", action="store_true")
     parser.add_argument("--no-model", action="store_true", help="skip the Qwen2-1.5B decode tok/s section")
+    parser.add_argument("--profile-case", choices=["gemv", "gemm"],
+                        help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
+                             "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv) or M=2048 (gemm)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.profile_case:
+        profile_case(args.profile_case)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -468,7 +491,7 @@ def main() -> None:
     else:
         hbm_peak, peak_src, tensor_peak = 6650.0, "fallback", 1590.0
     traffic = load_traffic().get("gemv_gate_m1_bytes_per_launch")
-    roofline = {"bound": "hbm", "kernel": "w4g64_gemv_kernel (gate 1536->8960, M=1)",
+    roofline = {"bound": "hbm", "kernel": "gemv_mma_kernel (gate 1536->8960, M=1)",
                 "achieved": gate["GBps"], "peak": hbm_peak, "unit": "GB/s",
                 "frac": gate["GBps"] / hbm_peak, "peak_source": peak_src,
                 "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False)}
