@@ -126,10 +126,11 @@ QI4_API int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, c
                                          void* stream);
 
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
- * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128) and
- * K-split factor (CTAs per cluster, 1..8). rows = 0 restores the library's
- * own choice. No reference counterpart. */
-QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit);
+ * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
+ * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4 or 8, at
+ * least rows / 16). rows = 0 restores the library's own choice. No reference
+ * counterpart. */
+QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps);
 
 /* Reads and clears the device-side error flags of the kernels (a bounded
  * wait that timed out records QI4_DEVICE_WAIT_TIMEOUT). Synchronises

@@ -282,17 +282,18 @@ int qi4_gemv_plan_override(int lanes_per_row, int warps, int ksplit, int depth) 
   return QI4_OK;
 }
 
-int qi4_gemv_mma_plan_override(int rows, int ksplit) {
+int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps) {
   clear_error();
   if (rows == 0) {
-    set_gemv_mma_override(0, 0);
+    set_gemv_mma_override(0, 0, 0);
     return QI4_OK;
   }
-  if ((rows != 16 && rows != 32 && rows != 64 && rows != 128) || ksplit < 1 || ksplit > 8) {
-    set_error("invalid GEMV plan override (rows %d, ksplit %d)", rows, ksplit);
+  if ((rows != 16 && rows != 32 && rows != 64 && rows != 128) || ksplit < 1 || ksplit > 8 ||
+      (warps != 2 && warps != 4 && warps != 8) || rows / 16 > warps) {
+    set_error("invalid GEMV plan override (rows %d, ksplit %d, warps %d)", rows, ksplit, warps);
     return QI4_ERR_ARGUMENT;
   }
-  set_gemv_mma_override(rows, ksplit);
+  set_gemv_mma_override(rows, ksplit, warps);
   return QI4_OK;
 }
 

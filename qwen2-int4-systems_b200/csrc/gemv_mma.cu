@@ -61,8 +61,10 @@ struct Args {
   int out_dtype;
   int64_t N;
   int rows;             // R
+  int rows_log2;
   int boxes_per_split;  // boxes along K per CTA
   int G;                // groups per row (K / 64)
+  uint32_t mul4, mul8, mul12;  // 2^28, 2^24, 2^20 (right shifts by 4, 8, 12 as mul.hi)
 };
 
 struct TableEntry {
@@ -108,14 +110,46 @@ __device__ __forceinline__ uint32_t nibble_pair(uint32_t w_shifted) {
   return d;
 }
 
+#ifndef QI4_GEMV_VARIANT
+#define QI4_GEMV_VARIANT 0
+#endif
+// bit 0: right shifts as mul.hi (FMA pipe); bit 1: zero point through an MMA
+// of the constant -(magic + 8 + z) fragment instead of packed subtracts.
+template <int XT>
+__host__ __device__ constexpr int variant() {
+  return XT == QI4_DTYPE_F16 ? (QI4_GEMV_VARIANT & 1) : QI4_GEMV_VARIANT;
+}
+
+__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // Word w (8 codes) -> four operand registers holding code pairs
 // (i, i+4), i = 0..3, each minus (magic + 8 + z) = exact (c - z).
 template <int XT>
-__device__ __forceinline__ void expand_word(uint32_t w, uint32_t zc2, uint32_t* r) {
-  r[0] = sub2<XT>(nibble_pair<XT>(w), zc2);
-  r[1] = sub2<XT>(nibble_pair<XT>(w >> 4), zc2);
-  r[2] = sub2<XT>(nibble_pair<XT>(w >> 8), zc2);
-  r[3] = sub2<XT>(nibble_pair<XT>(w >> 12), zc2);
+__device__ __forceinline__ void expand_word(uint32_t w, uint32_t zc2, uint32_t* r, uint32_t m4, uint32_t m8,
+                                            uint32_t m12) {
+  constexpr int V = variant<XT>();
+  uint32_t w1, w2, w3;
+  if constexpr (V & 1) {
+    w1 = mulhi(w, m4);
+    w2 = mulhi(w, m8);
+    w3 = mulhi(w, m12);
+  } else {
+    w1 = w >> 4;
+    w2 = w >> 8;
+    w3 = w >> 12;
+  }
+  r[0] = nibble_pair<XT>(w);
+  r[1] = nibble_pair<XT>(w1);
+  r[2] = nibble_pair<XT>(w2);
+  r[3] = nibble_pair<XT>(w3);
+  if constexpr (!(V & 2)) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) r[i] = sub2<XT>(r[i], zc2);
+  }
 }
 
 // Packed (magic + 8 + z, magic + 8 + z) in the operand type (exact integers).
@@ -161,67 +195,105 @@ __device__ __forceinline__ uint32_t prmt_hi(uint32_t a, uint32_t b) {  // (a.hi1
   return d;
 }
 
-// Activations of one token for one group, as the lane's B fragments: the 16
-// elements x[16 tq .. 16 tq + 15] of the group, read straight from global
-// memory (L2) and permuted into the k order of the weight fragments, which
-// pair codes (i, i+4): k-step s takes elements {0,4,1,5} + 2s (s < 2) and
-// {8,12,9,13} + 2(s-2). FP32 activations become a bf16 hi and lo pair.
-struct XRaw {
-  uint4 q[4];  // 16 elements: 2 x uint4 for 16-bit types, 4 x float4 for FP32
-};
-
+// Activations are staged once per CTA in shared memory, right after the
+// dependency wait (one round trip to L2 for the whole K slice), already in
+// the k order of the weight fragments. Those pair codes (i, i+4) of each
+// 8-code word, so within every 8 consecutive elements the staged order is
+// x0 x4 x1 x5 x2 x6 x3 x7 and each B register of a k-step is one aligned
+// 32-bit word: lane tq of token t reads its 16 elements of group g as two
+// 16-byte words at t * xstride + 128 g + 32 tq. FP32 activations are staged
+// as a bf16 hi plane followed by a lo plane (x - hi, rounded), 128 gs bytes
+// each. The token stride is padded by 16 bytes so that the 8 tokens of a
+// quarter-warp hit distinct banks.
 template <int XT>
-__device__ __forceinline__ void load_x(const void* x, int64_t idx, XRaw& r) {
-  if constexpr (XT == QI4_DTYPE_F32) {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + idx);
+__device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride, int g0, int gs, int tid,
+                                        int nthreads) {
+  const int per_tok = gs * 8;  // 8-element chunks per token
+  const uint32_t base = smem_addr(xs);
+  // One flat loop over (token, chunk), unrolled so that the loads of several
+  // iterations are in flight together (one round trip to L2 in total).
+#pragma unroll 4
+  for (int i = tid; i < a.M * per_tok; i += nthreads) {
+    const int tok = i / per_tok, c = i - tok * per_tok;
+    {
+      const int64_t e = (int64_t)tok * a.K + (int64_t)g0 * kGroup + (int64_t)c * 8;
+      uint32_t w[4];
+      if constexpr (XT == QI4_DTYPE_F32) {
+        const float4 v0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e));
+        const float4 v1 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e) + 1);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t l[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) r.q[q] = __ldg(p + q);
-  } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(x) + idx);
-    r.q[0] = __ldg(p);
-    r.q[1] = __ldg(p + 1);
-  }
-}
-
-__device__ __forceinline__ void zero_x(XRaw& r) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) r.q[q] = make_uint4(0, 0, 0, 0);
-}
-
-// b[2s], b[2s+1]: the two B registers of k-step s (hi part); lo likewise.
-template <int XT>
-__device__ __forceinline__ void x_frags(const XRaw& r, uint32_t (&hi)[8], uint32_t (&lo)[8]) {
-  uint32_t w[8], l[8];
-  if constexpr (XT == QI4_DTYPE_F32) {
-    const float* v = reinterpret_cast<const float*>(r.q);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      w[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
-      l[q] = pack_bf16x2(v[2 * q] - __uint_as_float(w[q] << 16), v[2 * q + 1] - __uint_as_float(w[q] & 0xFFFF0000u));
+        for (int q = 0; q < 4; ++q) {
+          w[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
+          l[q] = pack_bf16x2(v[2 * q] - __uint_as_float(w[q] << 16),
+                             v[2 * q + 1] - __uint_as_float(w[q] & 0xFFFF0000u));
+        }
+        sts128(base + tok * xstride + gs * 128 + c * 16,
+               make_uint4(prmt_lo(l[0], l[2]), prmt_hi(l[0], l[2]), prmt_lo(l[1], l[3]), prmt_hi(l[1], l[3])));
+      } else {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(a.x) + e));
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+      }
+      sts128(base + tok * xstride + c * 16,
+             make_uint4(prmt_lo(w[0], w[2]), prmt_hi(w[0], w[2]), prmt_lo(w[1], w[3]), prmt_hi(w[1], w[3])));
     }
-  } else {
-    w[0] = r.q[0].x; w[1] = r.q[0].y; w[2] = r.q[0].z; w[3] = r.q[0].w;
-    w[4] = r.q[1].x; w[5] = r.q[1].y; w[6] = r.q[1].z; w[7] = r.q[1].w;
-  }
-  hi[0] = prmt_lo(w[0], w[2]); hi[1] = prmt_hi(w[0], w[2]);
-  hi[2] = prmt_lo(w[1], w[3]); hi[3] = prmt_hi(w[1], w[3]);
-  hi[4] = prmt_lo(w[4], w[6]); hi[5] = prmt_hi(w[4], w[6]);
-  hi[6] = prmt_lo(w[5], w[7]); hi[7] = prmt_hi(w[5], w[7]);
-  if constexpr (XT == QI4_DTYPE_F32) {
-    lo[0] = prmt_lo(l[0], l[2]); lo[1] = prmt_hi(l[0], l[2]);
-    lo[2] = prmt_lo(l[1], l[3]); lo[3] = prmt_hi(l[1], l[3]);
-    lo[4] = prmt_lo(l[4], l[6]); lo[5] = prmt_hi(l[4], l[6]);
-    lo[6] = prmt_lo(l[5], l[7]); lo[7] = prmt_hi(l[5], l[7]);
   }
 }
 
-template <int XT, int NT>
-__global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap, const Args a) {
+__host__ __device__ constexpr int x_stride_bytes(int bps, bool f32) { return bps * kGroupsPerBox * 128 * (f32 ? 2 : 1) + 16; }
+
+// Scale / zero-point table of the CTA's slab, built before the dependency
+// wait: entry (r, g) = {scale as float, packed (magic + 8 + z) pair}. Scales
+// and zero points of four consecutive groups of a row are one 8-byte and one
+// 2-byte load when the row length in groups is a multiple of four.
+template <int XT>
+__device__ __forceinline__ void build_table(const Args& a, TableEntry* table, int tstride, int64_t row0, int g0,
+                                            int gs, int tid, int nthreads) {
+  const int R = a.rows;
+  const int nch = (gs + 3) >> 2;
+  const bool vec = (a.G & 3) == 0;
+  for (int e = tid; e < R * nch; e += nthreads) {
+    const int r = e & (R - 1), g = (e >> a.rows_log2) << 2;
+    const int64_t row = row0 + r;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t znib = 0;  // the four groups' stored zero nibbles (two's complement; 0 when absent)
+    if (row < a.N) {
+      const int64_t gi = row * a.G + g0 + g;
+      if (vec && g + 4 <= gs) {
+        const uint2 sv = __ldg(reinterpret_cast<const uint2*>(a.scales + gi));
+        const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
+        const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
+        s[0] = s01.x; s[1] = s01.y; s[2] = s23.x; s[3] = s23.y;
+        if (a.zeros) znib = __ldg(reinterpret_cast<const unsigned short*>(a.zeros + (gi >> 1)));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (g + j < gs) {
+            s[j] = __half2float(__ldg(a.scales + gi + j));
+            if (a.zeros) znib |= (uint32_t)((__ldg(a.zeros + ((gi + j) >> 1)) >> (((gi + j) & 1) * 4)) & 0xF) << (4 * j);
+          }
+        }
+      }
+    }
+    TableEntry* t = table + r * tstride + g;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (g + j < gs)
+        t[j] = TableEntry{s[j], (Fmt<XT>::kMagic + (((znib >> (4 * j)) & 0xF) ^ 0x8u) * 0x00010001u) |
+                                    ((variant<XT>() & 2) ? 0x80008000u : 0u)};
+  }
+}
+
+template <int XT, int NT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap, const Args a) {
+  constexpr int kThr = WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int R = a.rows;
-  const int RB = R >> 4;  // 16-row blocks
+  const int RB = R >> 4;      // 16-row blocks
+  const int KP = WARPS / RB;  // warps that share one 16-row block
   const int nbox_total = (a.G + kGroupsPerBox - 1) / kGroupsPerBox;
   const int box0 = blockIdx.y * a.boxes_per_split;
   const int nbox = min(a.boxes_per_split, nbox_total - box0);
@@ -230,54 +302,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
   const int64_t row0 = (int64_t)blockIdx.x * R;
 
   const int tstride = a.boxes_per_split * kGroupsPerBox + 1;  // odd stride: conflict-free table reads
-  const int KP = (kThreads / 32) / RB;                         // warps that share one 16-row block
   uint8_t* wsm = smem;                                         // nbox x R x 128
   TableEntry* table = reinterpret_cast<TableEntry*>(wsm + (size_t)a.boxes_per_split * R * kBoxBytes);
   float* red = reinterpret_cast<float*>(table + (size_t)R * tstride);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(red + (size_t)(KP - 1) * RB * 32 * NT * 4 + (size_t)R * NT * 8);
+  uint8_t* xs = reinterpret_cast<uint8_t*>(red + (size_t)(KP - 1) * RB * 32 * NT * 4 + (size_t)R * NT * 8);
+  const int xstride = x_stride_bytes(a.boxes_per_split, XT == QI4_DTYPE_F32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xs + (size_t)a.M * xstride);
 
   // Everything that depends only on the weights happens before
-  // griddepcontrol.wait, overlapping the previous kernel of a chain.
+  // griddepcontrol.wait, overlapping the previous kernels of a chain.
   pdl_launch_dependents();
   const int tid = threadIdx.x;
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
   if (tid == 0 && nbox > 0) {
-    prefetch_tensor_map(&wmap);
-    mbar_arrive_expect_tx(bar, (uint32_t)(nbox * R * kBoxBytes));
-    for (int b = 0; b < nbox; ++b)
-      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, &wmap, (box0 + b) * kBoxBytes, (int)row0, bar);
-  }
-  const int entries = R * gs;
-  for (int e = tid; e < entries; e += kThreads) {
-    const int r = e / gs, g = e - r * gs;
-    const int64_t row = row0 + r;
-    float sv = 0.f;
-    int z = 0;
-    if (row < a.N) {
-      const int64_t gi = row * a.G + g0 + g;
-      sv = __half2float(__ldg(a.scales + gi));
-      z = load_zero(a.zeros, gi);
+    for (int b = 0; b < nbox; ++b) mbar_init(bars + b, 1);
+    fence_barrier_init();
+    for (int b = 0; b < nbox; ++b) {
+      mbar_arrive_expect_tx(bars + b, (uint32_t)(R * kBoxBytes));
+      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, &wmap, (box0 + b) * kBoxBytes, (int)row0, bars + b);
     }
-    table[r * tstride + g] = TableEntry{sv, zero_code<XT>(z)};
   }
-  __syncthreads();
+  build_table<XT>(a, table, tstride, row0, g0, gs, tid, kThr);
+  __syncthreads();  // barriers initialised, table complete
 
   const int warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;  // MMA groupID / thread-in-group
   const int rb = warp % RB, kp = warp / RB;
   const int gb = (gs * kp) / KP, ge = (gs * (kp + 1)) / KP;  // this warp's groups
-  if (nbox > 0 && ge > gb) mbar_wait(bar, 0, &g_gemv_mma_error);
 
   pdl_wait();  // activations come from the previous kernel
+  stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
+  __syncthreads();
 
   const int r_lo = rb * 16 + gq;
   // Rows r and r + 8 share r % 8 (the swizzle phase): the lane's 8 bytes of
   // group g sit in 16-byte chunk (2 (g % 4) + tq / 2) XOR (r % 8), half tq % 2.
   const uint32_t a_row = smem_addr(wsm) + r_lo * kBoxBytes + ((tq & 1) << 3);
+  const uint32_t x_lane = smem_addr(xs) + gq * xstride + tq * 32;
   const TableEntry* t_lo = table + r_lo * tstride;
   const TableEntry* t_hi = t_lo + 8 * tstride;
 
@@ -287,37 +347,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
 
-  constexpr int kBatch = 4;  // groups whose activations are in flight together
-  for (int gbat = gb; gbat < ge; gbat += kBatch) {
-    XRaw xr[kBatch][NT];
+  uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j)
+  for (int j = 0; j < 4; ++j) coff[j] = (uint32_t)((((j << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
+  for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
+    // Each box has its own barrier: the first groups are used while later
+    // boxes are still in flight.
+    mbar_wait(bars + b, 0, &g_gemv_mma_error);
+    const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        const int tok = n * 8 + gq;
-        if (gbat + j < ge && tok < a.M)
-          load_x<XT>(a.x, (int64_t)tok * a.K + (int64_t)(g0 + gbat + j) * kGroup + 16 * tq, xr[j][n]);
-        else
-          zero_x(xr[j][n]);
-      }
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int g = gbat + j;
-      if (g >= ge) break;
-      const int chunk = ((((g & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4;
-      const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes + chunk);
-      const uint2 wl = lds64(ap);
-      const uint2 wh = lds64(ap + 8 * kBoxBytes);
+    for (int j = 0; j < 4; ++j) {
+      const int g = 4 * b + j;
+      if (g < gb || g >= ge) continue;
+      const uint2 wl = lds64(box + coff[j]);
+      const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
       const TableEntry el = t_lo[g], eh = t_hi[g];
       uint32_t al[8], ah[8];
-      expand_word<XT>(wl.x, el.zc2, al);
-      expand_word<XT>(wl.y, el.zc2, al + 4);
-      expand_word<XT>(wh.x, eh.zc2, ah);
-      expand_word<XT>(wh.y, eh.zc2, ah + 4);
+      expand_word<XT>(wl.x, el.zc2, al, a.mul4, a.mul8, a.mul12);
+      expand_word<XT>(wl.y, el.zc2, al + 4, a.mul4, a.mul8, a.mul12);
+      expand_word<XT>(wh.x, eh.zc2, ah, a.mul4, a.mul8, a.mul12);
+      expand_word<XT>(wh.y, eh.zc2, ah + 4, a.mul4, a.mul8, a.mul12);
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
-        uint32_t bh[8], bl[8];
-        x_frags<XT>(xr[j][n], bh, bl);
+        uint4 xb[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
+                       make_uint4(0, 0, 0, 0)};
+        if (n * 8 + gq < a.M) {
+          const uint32_t xp = x_lane + (uint32_t)(n * 8 * xstride + g * 128);
+          xb[0] = lds128(xp);
+          xb[1] = lds128(xp + 16);
+          if constexpr (XT == QI4_DTYPE_F32) {
+            xb[2] = lds128(xp + gs * 128);
+            xb[3] = lds128(xp + gs * 128 + 16);
+          }
+        }
+        const uint32_t bh[8] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w, xb[1].x, xb[1].y, xb[1].z, xb[1].w};
+        const uint32_t bl[8] = {xb[2].x, xb[2].y, xb[2].z, xb[2].w, xb[3].x, xb[3].y, xb[3].z, xb[3].w};
         float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int st = 0; st < 4; ++st) {
@@ -333,55 +397,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
     }
   }
 
-  // Reduce the KP warps of each row block through shared memory.
-  if (KP > 1) {
-    if (kp > 0) {
-      float* dst = red + (((size_t)(kp - 1) * RB + rb) * 32 + lane) * NT * 4;
+  // Every warp leaves its partial sums in shared memory ([kp][row][token]);
+  // then one thread per (row, token) adds the KP partials (independent loads,
+  // one round of latency) and stores the output, or, when K is split across a
+  // cluster, keeps the CTA's sum for the cluster reduction below.
+  float* part = red;  // [KP][R][NT * 8]
+  const int ld = NT * 8;
 #pragma unroll
-      for (int n = 0; n < NT; ++n)
+  for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) dst[n * 4 + q] = acc[n][q];
-    }
-    __syncthreads();
-    if (kp == 0) {
-      for (int q2 = 1; q2 < KP; ++q2) {
-        const float* src = red + (((size_t)(q2 - 1) * RB + rb) * 32 + lane) * NT * 4;
-#pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) acc[n][q] += src[n * 4 + q];
-      }
-    }
-  }
-
+    for (int q = 0; q < 4; ++q)
+      part[((size_t)kp * R + r_lo + (q < 2 ? 0 : 8)) * ld + n * 8 + 2 * tq + (q & 1)] = acc[n][q];
+  __syncthreads();
   const bool split = gridDim.y > 1;
-  float* part = red + (size_t)(KP - 1) * RB * 32 * NT * 4;  // [R][NT*8] CTA partials for the cluster
-  if (kp == 0) {
+  for (int i = tid; i < R * a.M; i += kThr) {
+    const int tok = i / R, r = i - tok * R;
+    float sum = 0.f;
 #pragma unroll
-    for (int n = 0; n < NT; ++n) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = r_lo + (q < 2 ? 0 : 8);
-        const int tok = n * 8 + 2 * tq + (q & 1);
-        if (split) {
-          part[r * NT * 8 + tok] = acc[n][q];
-        } else {
-          const int64_t row = row0 + r;
-          if (tok < a.M && row < a.N) {
-            const float bv = a.bias ? load_as_f32(a.bias, a.bias_dtype, row) : 0.f;
-            store_from_f32(a.out, a.out_dtype, (int64_t)tok * a.N + row, acc[n][q] + bv);
-          }
-        }
+    for (int q = 0; q < 8; ++q)
+      if (q < KP) sum += part[((size_t)q * R + r) * ld + tok];
+    if (split) {
+      part[(size_t)r * ld + tok] = sum;
+    } else {
+      const int64_t row = row0 + r;
+      if (row < a.N) {
+        const float bv = a.bias ? load_as_f32(a.bias, a.bias_dtype, row) : 0.f;
+        store_from_f32(a.out, a.out_dtype, (int64_t)tok * a.N + row, sum + bv);
       }
     }
   }
   if (!split) return;
 
+  // Split K: the cluster's CTAs reduce over distributed shared memory, each
+  // CTA finishing an equal share of the slab's outputs.
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
-  if (cluster.block_rank() == 0) {
+  {
     const int nranks = (int)cluster.num_blocks();
-    for (int i = tid; i < R * NT * 8; i += kThreads) {
+    const int me = (int)cluster.block_rank();
+    const int total = R * NT * 8;
+    const int per = (total + nranks - 1) / nranks;
+    const int lo = me * per, hi = min(total, lo + per);
+    for (int i = lo + tid; i < hi; i += kThr) {
       const int r = i / (NT * 8), tok = i - r * (NT * 8);
       const int64_t row = row0 + r;
       if (tok >= a.M || row >= a.N) continue;
@@ -394,19 +451,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const __grid_cons
   cluster.sync();
 }
 
-size_t smem_bytes(int R, int bps, int NT, int M, int x_dtype) {
+size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32) {
   const int RB = R / 16;
-  const int KP = (kThreads / 32) / RB > 0 ? (kThreads / 32) / RB : 1;
+  const int KP = warps / RB > 0 ? warps / RB : 1;
   const size_t table = (size_t)R * (bps * kGroupsPerBox + 1) * sizeof(TableEntry);
-  (void)M;
-  (void)x_dtype;
   const size_t red = ((size_t)(KP - 1) * RB * 32 * NT * 4 + (size_t)R * NT * 8) * sizeof(float);
-  return 1024 + (size_t)bps * R * kBoxBytes + table + red + 16;
+  const size_t xs = (size_t)M * x_stride_bytes(bps, f32);
+  return 1024 + (size_t)bps * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
 }
 
-template <int XT, int NT>
+template <int XT, int NT, int WARPS>
 cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
-  auto kernel = gemv_mma_kernel<XT, NT>;
+  auto kernel = gemv_mma_kernel<XT, NT, WARPS>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -420,8 +476,8 @@ cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStre
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((a.N + a.rows - 1) / a.rows), (unsigned)ksplit, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes(a.rows, a.boxes_per_split, NT, a.M, XT);
+  cfg.blockDim = dim3(WARPS * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem_bytes(a.rows, WARPS, a.boxes_per_split, NT, a.M, XT == QI4_DTYPE_F32);
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int n = 0;
@@ -440,58 +496,64 @@ cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStre
   return cudaLaunchKernelEx(&cfg, kernel, map, a);
 }
 
+template <int XT, int NT>
+cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int ksplit, cudaStream_t s, bool pdl) {
+  switch (warps) {
+    case 2: return launch_t<XT, NT, 2>(map, a, ksplit, s, pdl);
+    case 4: return launch_t<XT, NT, 4>(map, a, ksplit, s, pdl);
+    default: return launch_t<XT, NT, 8>(map, a, ksplit, s, pdl);
+  }
+}
+
 template <int XT>
-cudaError_t launch_x(const CUtensorMap& map, const Args& a, int nt, int ksplit, cudaStream_t s, bool pdl) {
-  return nt <= 1 ? launch_t<XT, 1>(map, a, ksplit, s, pdl) : launch_t<XT, 2>(map, a, ksplit, s, pdl);
+cudaError_t launch_x(const CUtensorMap& map, const Args& a, int nt, int warps, int ksplit, cudaStream_t s,
+                     bool pdl) {
+  return nt <= 1 ? launch_w<XT, 1>(map, a, warps, ksplit, s, pdl) : launch_w<XT, 2>(map, a, warps, ksplit, s, pdl);
 }
 
 thread_local MmaGemvPlan g_override{};
 
 }  // namespace
 
-void set_gemv_mma_override(int rows, int ksplit) {
+void set_gemv_mma_override(int rows, int ksplit, int warps) {
   g_override = MmaGemvPlan{};
   g_override.rows = rows;
   g_override.ksplit = ksplit;
+  g_override.warps = warps;
 }
 
 MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms) {
-  MmaGemvPlan best{};
   const int G = (int)(K / kGroup);
   const int nboxes = (G + kGroupsPerBox - 1) / kGroupsPerBox;
   const int nt = M <= 8 ? 1 : 2;
-  auto make = [&](int R, int ks) {
+  auto make = [&](int R, int ks, int warps) {
     MmaGemvPlan p{};
     p.rows = R;
     p.ksplit = ks;
+    p.warps = warps;
     p.boxes_per_split = (nboxes + ks - 1) / ks;
     p.nt = nt;
-    p.smem = smem_bytes(R, p.boxes_per_split, nt, (int)M, x_dtype);
+    p.smem = smem_bytes(R, warps, p.boxes_per_split, nt, (int)M, x_dtype == QI4_DTYPE_F32);
     return p;
   };
   if (g_override.rows) {
-    MmaGemvPlan p = make(g_override.rows, g_override.ksplit);
+    const int w = g_override.warps ? g_override.warps : 4;
+    if (g_override.rows / 16 > w) return MmaGemvPlan{};
+    MmaGemvPlan p = make(g_override.rows, std::min(g_override.ksplit, nboxes), w);
     return p.smem <= 200 * 1024 ? p : MmaGemvPlan{};
   }
-  // Measured on B200 over Qwen2-1.5B shapes (chains of PDL launches): keep at
-  // least ~1.5 CTAs per SM (the largest row tile that does so wins, else 16
-  // rows), keep K whole for M <= 4, and for wider token tiles on long rows
-  // split K so that each CTA holds about seven 128-byte boxes.
-  int R = 16;
-  for (int cand : {64, 32})
-    if ((N + cand - 1) / cand >= (int64_t)(1.5 * num_sms)) {
-      R = cand;
-      break;
-    }
-  int ks = 1;
-  if (M > 4 && nboxes >= 16) ks = std::min(8, std::max(1, (nboxes + 6) / 7));
-  while (ks > 1 && (nboxes + (nboxes + ks - 1) / ks - 1) / ((nboxes + ks - 1) / ks) != ks) --ks;
-  best = make(R, ks);
-  while (best.smem > 100 * 1024 && best.ksplit < 8 && best.ksplit < nboxes) best = make(R, best.ksplit + 1);
-  if (best.rows == 0) {
-    best = make(16, std::min(8, nboxes));
-    if (best.smem > 200 * 1024) best = MmaGemvPlan{};
-  }
+  // Measured on B200 over Qwen2-1.5B shapes (chains of 28 PDL launches,
+  // M = 1..16): 8 warps per CTA; 16-row tiles up to M = 8 and 32-row tiles
+  // beyond (the activation fragments are then shared by more weight rows);
+  // K whole for M < 4, else split over a cluster of two once a row holds at
+  // least 16 boxes; more splits only as shared memory requires (the staged
+  // activations grow with M).
+  (void)num_sms;
+  const int R = M > 8 ? 32 : 16;
+  int ks = (M >= 4 && nboxes >= 16) ? 2 : 1;
+  MmaGemvPlan best = make(R, ks, 8);
+  while (best.smem > 160 * 1024 && best.ksplit < 8 && best.ksplit < nboxes) best = make(R, best.ksplit + 1, 8);
+  if (best.smem > 200 * 1024) best = MmaGemvPlan{};
   return best;
 }
 
@@ -516,12 +578,16 @@ cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, co
   a.out_dtype = x_dtype;
   a.N = N;
   a.rows = p.rows;
+  a.rows_log2 = __builtin_ctz((unsigned)p.rows);
   a.boxes_per_split = p.boxes_per_split;
   a.G = (int)(K / kGroup);
+  a.mul4 = 1u << 28;
+  a.mul8 = 1u << 24;
+  a.mul12 = 1u << 20;
   switch (x_dtype) {
-    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.ksplit, stream, pdl);
-    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.ksplit, stream, pdl);
-    default: return launch_x<QI4_DTYPE_F32>(map, a, p.nt, p.ksplit, stream, pdl);
+    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
+    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
+    default: return launch_x<QI4_DTYPE_F32>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
   }
 }
 

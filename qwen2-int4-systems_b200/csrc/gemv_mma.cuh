@@ -8,8 +8,9 @@
 namespace qi4 {
 
 struct MmaGemvPlan {
-  int rows;             // output rows per CTA: 16, 32 or 64
+  int rows;             // output rows per CTA: 16, 32, 64 or 128
   int ksplit;           // CTAs per cluster along K (1..8)
+  int warps;            // warps per CTA: 2, 4 or 8 (rows / 16 <= warps)
   int boxes_per_split;  // 128-byte (4-group) boxes of K per CTA
   int nt;               // n8 token tiles: 1 (M <= 8) or 2 (M <= 16)
   size_t smem;
@@ -17,7 +18,7 @@ struct MmaGemvPlan {
 
 bool gemv_mma_supported(int64_t M, int64_t K);
 MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms);
-void set_gemv_mma_override(int rows, int ksplit);  // rows = 0 restores the model
+void set_gemv_mma_override(int rows, int ksplit, int warps);  // rows = 0 restores the model
 cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
                             const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
                             void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& plan);

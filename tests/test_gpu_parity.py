@@ -288,10 +288,10 @@ def test_wrong_device_mix_is_rejected(b200, cuda_device):
                                out_features=64, in_features=128, group_size=64, packing="canonical")
 
 
-@pytest.mark.parametrize("rows", [16, 32, 64, 128])
+@pytest.mark.parametrize(("rows", "warps"), [(16, 2), (16, 4), (32, 2), (32, 4), (64, 4), (64, 8), (128, 8)])
 @pytest.mark.parametrize("ksplit", [1, 2, 3, 5])
-def test_gemv_launch_shapes_agree(b200, cuda_device, rows, ksplit):
-    """Every forced launch shape (rows per CTA, cluster K split) gives the oracle's answer."""
+def test_gemv_launch_shapes_agree(b200, cuda_device, rows, warps, ksplit):
+    """Every forced launch shape (rows per CTA, warps, cluster K split) gives the oracle's answer."""
     from importlib import import_module
 
     lib = import_module(b200.__name__ + "._lib").load()
@@ -299,14 +299,14 @@ def test_gemv_launch_shapes_agree(b200, cuda_device, rows, ksplit):
     qw, sc, z = _weights(k, n, "asym", 21)
     x = torch.randn(5, k, generator=torch.Generator().manual_seed(22)).to(torch.bfloat16)
     ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=n, in_features=k, accumulate="f64")
-    assert lib.qi4_gemv_mma_plan_override(rows, ksplit) == 0
+    assert lib.qi4_gemv_mma_plan_override(rows, ksplit, warps) == 0
     try:
         got = b200.b200_w4g64_linear(
             x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
             out_features=n, in_features=k, group_size=64, packing="canonical", algo=ALGOS["gemv"])
     finally:
-        lib.qi4_gemv_mma_plan_override(0, 0)
-    assert_linear_close(got, ref, 1e-3, f"rows={rows} ksplit={ksplit}")
+        lib.qi4_gemv_mma_plan_override(0, 0, 0)
+    assert_linear_close(got, ref, 1e-3, f"rows={rows} warps={warps} ksplit={ksplit}")
 
 
 def test_device_status_clean_after_kernels(b200, cuda_device):
