@@ -127,10 +127,18 @@ QI4_API int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, c
 
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
- * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4 or 8, at
- * least rows / 16). rows = 0 restores the library's own choice. No reference
+ * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8 or 16,
+ * at least rows / 16). rows = 0 restores the library's own choice. No reference
  * counterpart. */
 QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps);
+
+/* Reports, without touching a GPU, the TMA/tensor-pipe GEMV launch plan the
+ * library would use for an M x K activation block, N output features and
+ * `num_sms` SMs: plan[0..4] = rows per CTA, K-split factor, warps per CTA,
+ * 128-byte K boxes per CTA, dynamic shared memory in bytes. Returns QI4_OK,
+ * or QI4_ERR_SHAPE when no plan exists (M outside 1..16 or K not a multiple of
+ * 64). Honours qi4_gemv_mma_plan_override. No reference counterpart. */
+QI4_API int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms, int64_t* plan);
 
 /* Reads and clears the device-side error flags of the kernels (a bounded
  * wait that timed out records QI4_DEVICE_WAIT_TIMEOUT). Synchronises

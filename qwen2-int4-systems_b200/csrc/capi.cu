@@ -282,6 +282,29 @@ int qi4_gemv_plan_override(int lanes_per_row, int warps, int ksplit, int depth) 
   return QI4_OK;
 }
 
+int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms, int64_t* plan) {
+  clear_error();
+  if (plan == nullptr || num_sms <= 0 || N <= 0) {
+    set_error("qi4_gemv_mma_plan: plan must be non-null, N and num_sms positive");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (!gemv_mma_supported(M, K)) {
+    set_error("qi4_gemv_mma_plan: no GEMV plan for M=%lld K=%lld", (long long)M, (long long)K);
+    return QI4_ERR_SHAPE;
+  }
+  const MmaGemvPlan p = plan_gemv_mma(M, N, K, x_dtype, num_sms);
+  if (p.rows == 0) {
+    set_error("qi4_gemv_mma_plan: no plan fits shared memory");
+    return QI4_ERR_SHAPE;
+  }
+  plan[0] = p.rows;
+  plan[1] = p.ksplit;
+  plan[2] = p.warps;
+  plan[3] = p.boxes_per_split;
+  plan[4] = (int64_t)p.smem;
+  return QI4_OK;
+}
+
 int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps) {
   clear_error();
   if (rows == 0) {
@@ -289,7 +312,7 @@ int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps) {
     return QI4_OK;
   }
   if ((rows != 16 && rows != 32 && rows != 64 && rows != 128) || ksplit < 1 || ksplit > 8 ||
-      (warps != 2 && warps != 4 && warps != 8) || rows / 16 > warps) {
+      (warps != 2 && warps != 4 && warps != 8 && warps != 16) || rows / 16 > warps) {
     set_error("invalid GEMV plan override (rows %d, ksplit %d, warps %d)", rows, ksplit, warps);
     return QI4_ERR_ARGUMENT;
   }

@@ -64,7 +64,6 @@ struct Args {
   int rows_log2;
   int boxes_per_split;  // boxes along K per CTA
   int G;                // groups per row (K / 64)
-  uint32_t mul4, mul8, mul12;  // 2^28, 2^24, 2^20 (right shifts by 4, 8, 12 as mul.hi)
 };
 
 struct TableEntry {
@@ -110,46 +109,14 @@ __device__ __forceinline__ uint32_t nibble_pair(uint32_t w_shifted) {
   return d;
 }
 
-#ifndef QI4_GEMV_VARIANT
-#define QI4_GEMV_VARIANT 0
-#endif
-// bit 0: right shifts as mul.hi (FMA pipe); bit 1: zero point through an MMA
-// of the constant -(magic + 8 + z) fragment instead of packed subtracts.
-template <int XT>
-__host__ __device__ constexpr int variant() {
-  return XT == QI4_DTYPE_F16 ? (QI4_GEMV_VARIANT & 1) : QI4_GEMV_VARIANT;
-}
-
-__device__ __forceinline__ uint32_t mulhi(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.hi.u32 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
 // Word w (8 codes) -> four operand registers holding code pairs
 // (i, i+4), i = 0..3, each minus (magic + 8 + z) = exact (c - z).
 template <int XT>
-__device__ __forceinline__ void expand_word(uint32_t w, uint32_t zc2, uint32_t* r, uint32_t m4, uint32_t m8,
-                                            uint32_t m12) {
-  constexpr int V = variant<XT>();
-  uint32_t w1, w2, w3;
-  if constexpr (V & 1) {
-    w1 = mulhi(w, m4);
-    w2 = mulhi(w, m8);
-    w3 = mulhi(w, m12);
-  } else {
-    w1 = w >> 4;
-    w2 = w >> 8;
-    w3 = w >> 12;
-  }
-  r[0] = nibble_pair<XT>(w);
-  r[1] = nibble_pair<XT>(w1);
-  r[2] = nibble_pair<XT>(w2);
-  r[3] = nibble_pair<XT>(w3);
-  if constexpr (!(V & 2)) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) r[i] = sub2<XT>(r[i], zc2);
-  }
+__device__ __forceinline__ void expand_word(uint32_t w, uint32_t zc2, uint32_t* r) {
+  r[0] = sub2<XT>(nibble_pair<XT>(w), zc2);
+  r[1] = sub2<XT>(nibble_pair<XT>(w >> 4), zc2);
+  r[2] = sub2<XT>(nibble_pair<XT>(w >> 8), zc2);
+  r[3] = sub2<XT>(nibble_pair<XT>(w >> 12), zc2);
 }
 
 // Packed (magic + 8 + z, magic + 8 + z) in the operand type (exact integers).
@@ -205,38 +172,62 @@ __device__ __forceinline__ uint32_t prmt_hi(uint32_t a, uint32_t b) {  // (a.hi1
 // as a bf16 hi plane followed by a lo plane (x - hi, rounded), 128 gs bytes
 // each. The token stride is padded by 16 bytes so that the 8 tokens of a
 // quarter-warp hit distinct banks.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 template <int XT>
 __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride, int g0, int gs, int tid,
                                         int nthreads) {
   const int per_tok = gs * 8;  // 8-element chunks per token
+  const int total = a.M * per_tok;
   const uint32_t base = smem_addr(xs);
-  // One flat loop over (token, chunk), unrolled so that the loads of several
-  // iterations are in flight together (one round trip to L2 in total).
+  if (XT != QI4_DTYPE_F32 && total <= nthreads) {
+    // One chunk per thread at most: load, permute, store.
+    if (tid < total) {
+      const int tok = tid / per_tok, c = tid - tok * per_tok;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(a.x) +
+                                                           (int64_t)tok * a.K + (int64_t)g0 * kGroup + c * 8));
+      sts128(base + tok * xstride + c * 16,
+             make_uint4(prmt_lo(v.x, v.z), prmt_hi(v.x, v.z), prmt_lo(v.y, v.w), prmt_hi(v.y, v.w)));
+    }
+  } else if constexpr (XT != QI4_DTYPE_F32) {
+    // Asynchronous 16-byte copies straight into place (all in flight at
+    // once), then each thread permutes the chunks it copied.
+    for (int i = tid; i < total; i += nthreads) {
+      const int tok = i / per_tok, c = i - tok * per_tok;
+      cp_async16(base + tok * xstride + c * 16,
+                 static_cast<const unsigned short*>(a.x) + (int64_t)tok * a.K + (int64_t)g0 * kGroup + c * 8);
+    }
+    cp_async_wait_all();
+    for (int i = tid; i < total; i += nthreads) {
+      const int tok = i / per_tok, c = i - tok * per_tok;
+      const uint32_t at = base + tok * xstride + c * 16;
+      const uint4 v = lds128(at);
+      sts128(at, make_uint4(prmt_lo(v.x, v.z), prmt_hi(v.x, v.z), prmt_lo(v.y, v.w), prmt_hi(v.y, v.w)));
+    }
+  } else {
+    // FP32: through registers (bf16 hi and lo planes), several loads in flight.
 #pragma unroll 4
-  for (int i = tid; i < a.M * per_tok; i += nthreads) {
-    const int tok = i / per_tok, c = i - tok * per_tok;
-    {
+    for (int i = tid; i < total; i += nthreads) {
+      const int tok = i / per_tok, c = i - tok * per_tok;
       const int64_t e = (int64_t)tok * a.K + (int64_t)g0 * kGroup + (int64_t)c * 8;
-      uint32_t w[4];
-      if constexpr (XT == QI4_DTYPE_F32) {
-        const float4 v0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e));
-        const float4 v1 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e) + 1);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint32_t l[4];
+      const float4 v0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e));
+      const float4 v1 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e) + 1);
+      const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      uint32_t w[4], l[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          w[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
-          l[q] = pack_bf16x2(v[2 * q] - __uint_as_float(w[q] << 16),
-                             v[2 * q + 1] - __uint_as_float(w[q] & 0xFFFF0000u));
-        }
-        sts128(base + tok * xstride + gs * 128 + c * 16,
-               make_uint4(prmt_lo(l[0], l[2]), prmt_hi(l[0], l[2]), prmt_lo(l[1], l[3]), prmt_hi(l[1], l[3])));
-      } else {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(a.x) + e));
-        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+      for (int q = 0; q < 4; ++q) {
+        w[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);
+        l[q] = pack_bf16x2(v[2 * q] - __uint_as_float(w[q] << 16), v[2 * q + 1] - __uint_as_float(w[q] & 0xFFFF0000u));
       }
       sts128(base + tok * xstride + c * 16,
              make_uint4(prmt_lo(w[0], w[2]), prmt_hi(w[0], w[2]), prmt_lo(w[1], w[3]), prmt_hi(w[1], w[3])));
+      sts128(base + tok * xstride + gs * 128 + c * 16,
+             make_uint4(prmt_lo(l[0], l[2]), prmt_hi(l[0], l[2]), prmt_lo(l[1], l[3]), prmt_hi(l[1], l[3])));
     }
   }
 }
@@ -280,8 +271,7 @@ __device__ __forceinline__ void build_table(const Args& a, TableEntry* table, in
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (g + j < gs)
-        t[j] = TableEntry{s[j], (Fmt<XT>::kMagic + (((znib >> (4 * j)) & 0xF) ^ 0x8u) * 0x00010001u) |
-                                    ((variant<XT>() & 2) ? 0x80008000u : 0u)};
+        t[j] = TableEntry{s[j], Fmt<XT>::kMagic + (((znib >> (4 * j)) & 0xF) ^ 0x8u) * 0x00010001u};
   }
 }
 
@@ -296,9 +286,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
   const int KP = WARPS / RB;  // warps that share one 16-row block
   const int nbox_total = (a.G + kGroupsPerBox - 1) / kGroupsPerBox;
   const int box0 = blockIdx.y * a.boxes_per_split;
-  const int nbox = min(a.boxes_per_split, nbox_total - box0);
+  const int nbox = max(0, min(a.boxes_per_split, nbox_total - box0));  // 0 only for a CTA past the end
   const int g0 = box0 * kGroupsPerBox;
-  const int gs = min(a.G - g0, nbox * kGroupsPerBox);  // groups of this CTA
+  const int gs = max(0, min(a.G - g0, nbox * kGroupsPerBox));  // groups of this CTA
   const int64_t row0 = (int64_t)blockIdx.x * R;
 
   const int tstride = a.boxes_per_split * kGroupsPerBox + 1;  // odd stride: conflict-free table reads
@@ -363,10 +353,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
       const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
       const TableEntry el = t_lo[g], eh = t_hi[g];
       uint32_t al[8], ah[8];
-      expand_word<XT>(wl.x, el.zc2, al, a.mul4, a.mul8, a.mul12);
-      expand_word<XT>(wl.y, el.zc2, al + 4, a.mul4, a.mul8, a.mul12);
-      expand_word<XT>(wh.x, eh.zc2, ah, a.mul4, a.mul8, a.mul12);
-      expand_word<XT>(wh.y, eh.zc2, ah + 4, a.mul4, a.mul8, a.mul12);
+      expand_word<XT>(wl.x, el.zc2, al);
+      expand_word<XT>(wl.y, el.zc2, al + 4);
+      expand_word<XT>(wh.x, eh.zc2, ah);
+      expand_word<XT>(wh.y, eh.zc2, ah + 4);
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         uint4 xb[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
@@ -414,7 +404,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
     const int tok = i / R, r = i - tok * R;
     float sum = 0.f;
 #pragma unroll
-    for (int q = 0; q < 8; ++q)
+    for (int q = 0; q < WARPS; ++q)  // KP <= WARPS
       if (q < KP) sum += part[((size_t)q * R + r) * ld + tok];
     if (split) {
       part[(size_t)r * ld + tok] = sum;
@@ -501,7 +491,8 @@ cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int kspli
   switch (warps) {
     case 2: return launch_t<XT, NT, 2>(map, a, ksplit, s, pdl);
     case 4: return launch_t<XT, NT, 4>(map, a, ksplit, s, pdl);
-    default: return launch_t<XT, NT, 8>(map, a, ksplit, s, pdl);
+    case 8: return launch_t<XT, NT, 8>(map, a, ksplit, s, pdl);
+    default: return launch_t<XT, NT, 16>(map, a, ksplit, s, pdl);
   }
 }
 
@@ -529,9 +520,9 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
   auto make = [&](int R, int ks, int warps) {
     MmaGemvPlan p{};
     p.rows = R;
-    p.ksplit = ks;
     p.warps = warps;
     p.boxes_per_split = (nboxes + ks - 1) / ks;
+    p.ksplit = (nboxes + p.boxes_per_split - 1) / p.boxes_per_split;  // every CTA gets at least one box
     p.nt = nt;
     p.smem = smem_bytes(R, warps, p.boxes_per_split, nt, (int)M, x_dtype == QI4_DTYPE_F32);
     return p;
@@ -543,16 +534,23 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
     return p.smem <= 200 * 1024 ? p : MmaGemvPlan{};
   }
   // Measured on B200 over Qwen2-1.5B shapes (chains of 28 PDL launches,
-  // M = 1..16): 8 warps per CTA; 16-row tiles up to M = 8 and 32-row tiles
-  // beyond (the activation fragments are then shared by more weight rows);
-  // K whole for M < 4, else split over a cluster of two once a row holds at
-  // least 16 boxes; more splits only as shared memory requires (the staged
-  // activations grow with M).
-  (void)num_sms;
-  const int R = M > 8 ? 32 : 16;
-  int ks = (M >= 4 && nboxes >= 16) ? 2 : 1;
-  MmaGemvPlan best = make(R, ks, 8);
-  while (best.smem > 160 * 1024 && best.ksplit < 8 && best.ksplit < nboxes) best = make(R, best.ksplit + 1, 8);
+  // M = 1..16): 8 warps per CTA; 16-row tiles below M = 8 and 32-row tiles
+  // from there (the activation fragments are then shared by more weight rows).
+  // K stays whole for M < 4 unless shared memory runs out. From M = 4 on, rows
+  // of at least 16 boxes are split over a cluster until the grid has 1.5 CTAs
+  // per SM, keeping each CTA within 110 KB so that two fit on an SM.
+  const int R = M >= 8 ? 32 : 16;
+  const int64_t tiles = (N + R - 1) / R;
+  // `req` is the requested split; make() may round it down to the number of
+  // CTAs that get boxes, so the loops step `req`, which always terminates.
+  int req = 1;
+  MmaGemvPlan best = make(R, req, 8);
+  if (M >= 4 && nboxes >= 16) {
+    while (req < 8 && req < nboxes &&
+           (tiles * best.ksplit < (int64_t)(1.5 * num_sms) || best.smem > 110 * 1024))
+      best = make(R, ++req, 8);
+  }
+  while (best.smem > 200 * 1024 && req < 8 && req < nboxes) best = make(R, ++req, 8);
   if (best.smem > 200 * 1024) best = MmaGemvPlan{};
   return best;
 }
@@ -581,9 +579,6 @@ cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, co
   a.rows_log2 = __builtin_ctz((unsigned)p.rows);
   a.boxes_per_split = p.boxes_per_split;
   a.G = (int)(K / kGroup);
-  a.mul4 = 1u << 28;
-  a.mul8 = 1u << 24;
-  a.mul12 = 1u << 20;
   switch (x_dtype) {
     case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
     case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);

@@ -10,7 +10,7 @@ namespace qi4 {
 struct MmaGemvPlan {
   int rows;             // output rows per CTA: 16, 32, 64 or 128
   int ksplit;           // CTAs per cluster along K (1..8)
-  int warps;            // warps per CTA: 2, 4 or 8 (rows / 16 <= warps)
+  int warps;            // warps per CTA: 2, 4, 8 or 16 (rows / 16 <= warps)
   int boxes_per_split;  // 128-byte (4-group) boxes of K per CTA
   int nt;               // n8 token tiles: 1 (M <= 8) or 2 (M <= 16)
   size_t smem;

@@ -288,7 +288,7 @@ def test_wrong_device_mix_is_rejected(b200, cuda_device):
                                out_features=64, in_features=128, group_size=64, packing="canonical")
 
 
-@pytest.mark.parametrize(("rows", "warps"), [(16, 2), (16, 4), (32, 2), (32, 4), (64, 4), (64, 8), (128, 8)])
+@pytest.mark.parametrize(("rows", "warps"), [(16, 2), (16, 4), (16, 16), (32, 2), (32, 4), (64, 4), (64, 8), (64, 16), (128, 8)])
 @pytest.mark.parametrize("ksplit", [1, 2, 3, 5])
 def test_gemv_launch_shapes_agree(b200, cuda_device, rows, warps, ksplit):
     """Every forced launch shape (rows per CTA, warps, cluster K split) gives the oracle's answer."""
