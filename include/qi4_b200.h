@@ -134,8 +134,9 @@ QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps);
 
 /* Reports, without touching a GPU, the TMA/tensor-pipe GEMV launch plan the
  * library would use for an M x K activation block, N output features and
- * `num_sms` SMs: plan[0..4] = rows per CTA, K-split factor, warps per CTA,
- * 128-byte K boxes per CTA, dynamic shared memory in bytes. Returns QI4_OK,
+ * `num_sms` SMs: plan[0..5] = rows per CTA, K-split factor, warps per CTA,
+ * 128-byte K boxes per CTA, dynamic shared memory in bytes, and 1 when the
+ * weight fragments are expanded before the dependency wait. Returns QI4_OK,
  * or QI4_ERR_SHAPE when no plan exists (M outside 1..16 or K not a multiple of
  * 64). Honours qi4_gemv_mma_plan_override. No reference counterpart. */
 QI4_API int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms, int64_t* plan);

@@ -302,6 +302,7 @@ int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms,
   plan[2] = p.warps;
   plan[3] = p.boxes_per_split;
   plan[4] = (int64_t)p.smem;
+  plan[5] = p.pre;
   return QI4_OK;
 }
 

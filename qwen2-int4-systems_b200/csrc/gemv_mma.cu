@@ -48,6 +48,7 @@ namespace {
 constexpr int kThreads = 256;   // 8 warps
 constexpr int kBoxBytes = 128;  // inner TMA box: 128 bytes = 256 codes = 4 groups
 constexpr int kGroupsPerBox = 4;
+constexpr int kPreGroups = 4;  // groups per warp expanded before the dependency wait
 
 struct Args {
   const void* x;
@@ -275,8 +276,45 @@ __device__ __forceinline__ void build_table(const Args& a, TableEntry* table, in
   }
 }
 
-template <int XT, int NT, int WARPS>
+// D = (c - z) . x for one group of 64 k and the lane's token tile(s), then
+// acc += scale * D (rows r and r + 8 of the lane; FP32 activations as two
+// MMAs of the bf16 hi and lo planes).
+template <int XT, int NT>
+__device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* al, const uint32_t* ah, float s_lo,
+                                          float s_hi, int g, int gq, int M, uint32_t x_lane, int xstride,
+                                          int gs) {
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    uint4 xb[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    if (n * 8 + gq < M) {
+      const uint32_t xp = x_lane + (uint32_t)(n * 8 * xstride + g * 128);
+      xb[0] = lds128(xp);
+      xb[1] = lds128(xp + 16);
+      if constexpr (XT == QI4_DTYPE_F32) {
+        xb[2] = lds128(xp + gs * 128);
+        xb[3] = lds128(xp + gs * 128 + 16);
+      }
+    }
+    const uint32_t bh[8] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w, xb[1].x, xb[1].y, xb[1].z, xb[1].w};
+    const uint32_t bl[8] = {xb[2].x, xb[2].y, xb[2].z, xb[2].w, xb[3].x, xb[3].y, xb[3].z, xb[3].w};
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int st = 0; st < 4; ++st) {
+      const uint32_t af[4] = {al[2 * st], ah[2 * st], al[2 * st + 1], ah[2 * st + 1]};
+      mma16816<XT>(d, af, bh[2 * st], bh[2 * st + 1]);
+      if constexpr (XT == QI4_DTYPE_F32) mma16816<XT>(d, af, bl[2 * st], bl[2 * st + 1]);
+    }
+    acc[n][0] = fmaf(s_lo, d[0], acc[n][0]);
+    acc[n][1] = fmaf(s_lo, d[1], acc[n][1]);
+    acc[n][2] = fmaf(s_hi, d[2], acc[n][2]);
+    acc[n][3] = fmaf(s_hi, d[3], acc[n][3]);
+  }
+}
+
+template <int XT, int NT, int WARPS, int PRE>
 __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap, const Args a) {
+  // PRE > 0: every warp has at most PRE groups, expanded into registers
+  // before the dependency wait (single-wave grids, whose CTAs start early).
   constexpr int kThr = WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -319,10 +357,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
   const int rb = warp % RB, kp = warp / RB;
   const int gb = (gs * kp) / KP, ge = (gs * (kp + 1)) / KP;  // this warp's groups
 
-  pdl_wait();  // activations come from the previous kernel
-  stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
-  __syncthreads();
-
   const int r_lo = rb * 16 + gq;
   // Rows r and r + 8 share r % 8 (the swizzle phase): the lane's 8 bytes of
   // group g sit in 16-byte chunk (2 (g % 4) + tq / 2) XOR (r % 8), half tq % 2.
@@ -337,52 +371,59 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[n][q] = 0.f;
 
-  uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
+  if constexpr (PRE > 0) {
+    uint32_t fa[PRE][16];
+    float fs[PRE][2];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) coff[j] = (uint32_t)((((j << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
-  for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
-    // Each box has its own barrier: the first groups are used while later
-    // boxes are still in flight.
-    mbar_wait(bars + b, 0, &g_gemv_mma_error);
-    const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
+    for (int j = 0; j < PRE; ++j) {
+      const int g = gb + j;
+      if (g < ge) {
+        mbar_wait(bars + (g >> 2), 0, &g_gemv_mma_error);
+        const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes) +
+                            (uint32_t)(((((g & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
+        const uint2 wl = lds64(ap);
+        const uint2 wh = lds64(ap + 8 * kBoxBytes);
+        const TableEntry el = t_lo[g], eh = t_hi[g];
+        expand_word<XT>(wl.x, el.zc2, fa[j]);
+        expand_word<XT>(wl.y, el.zc2, fa[j] + 4);
+        expand_word<XT>(wh.x, eh.zc2, fa[j] + 8);
+        expand_word<XT>(wh.y, eh.zc2, fa[j] + 12);
+        fs[j][0] = el.scale;
+        fs[j][1] = eh.scale;
+      }
+    }
+    pdl_wait();  // activations come from the previous kernel
+    stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
+    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int g = 4 * b + j;
-      if (g < gb || g >= ge) continue;
-      const uint2 wl = lds64(box + coff[j]);
-      const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
-      const TableEntry el = t_lo[g], eh = t_hi[g];
-      uint32_t al[8], ah[8];
-      expand_word<XT>(wl.x, el.zc2, al);
-      expand_word<XT>(wl.y, el.zc2, al + 4);
-      expand_word<XT>(wh.x, eh.zc2, ah);
-      expand_word<XT>(wh.y, eh.zc2, ah + 4);
+    for (int j = 0; j < PRE; ++j)
+      if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, gq, a.M, x_lane, xstride, gs);
+  } else {
+    pdl_wait();  // activations come from the previous kernel
+    stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
+    __syncthreads();
+
+    uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
 #pragma unroll
-      for (int n = 0; n < NT; ++n) {
-        uint4 xb[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0),
-                       make_uint4(0, 0, 0, 0)};
-        if (n * 8 + gq < a.M) {
-          const uint32_t xp = x_lane + (uint32_t)(n * 8 * xstride + g * 128);
-          xb[0] = lds128(xp);
-          xb[1] = lds128(xp + 16);
-          if constexpr (XT == QI4_DTYPE_F32) {
-            xb[2] = lds128(xp + gs * 128);
-            xb[3] = lds128(xp + gs * 128 + 16);
-          }
-        }
-        const uint32_t bh[8] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w, xb[1].x, xb[1].y, xb[1].z, xb[1].w};
-        const uint32_t bl[8] = {xb[2].x, xb[2].y, xb[2].z, xb[2].w, xb[3].x, xb[3].y, xb[3].z, xb[3].w};
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < 4; ++j) coff[j] = (uint32_t)((((j << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
+    for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
+      // Each box has its own barrier: the first groups are used while later
+      // boxes are still in flight.
+      mbar_wait(bars + b, 0, &g_gemv_mma_error);
+      const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
 #pragma unroll
-        for (int st = 0; st < 4; ++st) {
-          const uint32_t af[4] = {al[2 * st], ah[2 * st], al[2 * st + 1], ah[2 * st + 1]};
-          mma16816<XT>(d, af, bh[2 * st], bh[2 * st + 1]);
-          if constexpr (XT == QI4_DTYPE_F32) mma16816<XT>(d, af, bl[2 * st], bl[2 * st + 1]);
-        }
-        acc[n][0] = fmaf(el.scale, d[0], acc[n][0]);
-        acc[n][1] = fmaf(el.scale, d[1], acc[n][1]);
-        acc[n][2] = fmaf(eh.scale, d[2], acc[n][2]);
-        acc[n][3] = fmaf(eh.scale, d[3], acc[n][3]);
+      for (int j = 0; j < 4; ++j) {
+        const int g = 4 * b + j;
+        if (g < gb || g >= ge) continue;
+        const uint2 wl = lds64(box + coff[j]);
+        const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
+        const TableEntry el = t_lo[g], eh = t_hi[g];
+        uint32_t al[8], ah[8];
+        expand_word<XT>(wl.x, el.zc2, al);
+        expand_word<XT>(wl.y, el.zc2, al + 4);
+        expand_word<XT>(wh.x, eh.zc2, ah);
+        expand_word<XT>(wh.y, eh.zc2, ah + 4);
+        mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, gq, a.M, x_lane, xstride, gs);
       }
     }
   }
@@ -450,9 +491,9 @@ size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32) {
   return 1024 + (size_t)bps * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
 }
 
-template <int XT, int NT, int WARPS>
+template <int XT, int NT, int WARPS, int PRE>
 cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
-  auto kernel = gemv_mma_kernel<XT, NT, WARPS>;
+  auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -487,19 +528,21 @@ cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStre
 }
 
 template <int XT, int NT>
-cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int ksplit, cudaStream_t s, bool pdl) {
+cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int ksplit, int pre, cudaStream_t s,
+                     bool pdl) {
   switch (warps) {
-    case 2: return launch_t<XT, NT, 2>(map, a, ksplit, s, pdl);
-    case 4: return launch_t<XT, NT, 4>(map, a, ksplit, s, pdl);
-    case 8: return launch_t<XT, NT, 8>(map, a, ksplit, s, pdl);
-    default: return launch_t<XT, NT, 16>(map, a, ksplit, s, pdl);
+    case 2: return launch_t<XT, NT, 2, 0>(map, a, ksplit, s, pdl);
+    case 4: return launch_t<XT, NT, 4, 0>(map, a, ksplit, s, pdl);
+    case 8: return pre ? launch_t<XT, NT, 8, kPreGroups>(map, a, ksplit, s, pdl) : launch_t<XT, NT, 8, 0>(map, a, ksplit, s, pdl);
+    default: return launch_t<XT, NT, 16, 0>(map, a, ksplit, s, pdl);
   }
 }
 
 template <int XT>
-cudaError_t launch_x(const CUtensorMap& map, const Args& a, int nt, int warps, int ksplit, cudaStream_t s,
-                     bool pdl) {
-  return nt <= 1 ? launch_w<XT, 1>(map, a, warps, ksplit, s, pdl) : launch_w<XT, 2>(map, a, warps, ksplit, s, pdl);
+cudaError_t launch_x(const CUtensorMap& map, const Args& a, int nt, int warps, int ksplit, int pre,
+                     cudaStream_t s, bool pdl) {
+  return nt <= 1 ? launch_w<XT, 1>(map, a, warps, ksplit, pre, s, pdl)
+                 : launch_w<XT, 2>(map, a, warps, ksplit, pre, s, pdl);
 }
 
 thread_local MmaGemvPlan g_override{};
@@ -525,6 +568,12 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
     p.ksplit = (nboxes + p.boxes_per_split - 1) / p.boxes_per_split;  // every CTA gets at least one box
     p.nt = nt;
     p.smem = smem_bytes(R, warps, p.boxes_per_split, nt, (int)M, x_dtype == QI4_DTYPE_F32);
+    // A single-wave grid (one CTA per SM at most) starts ahead of the
+    // previous kernel's end; with at most kPreGroups groups per warp its
+    // weight fragments are expanded before the dependency wait.
+    const int kp = warps / (R / 16);
+    p.pre = warps == 8 && (N + R - 1) / R * p.ksplit <= num_sms &&
+            (p.boxes_per_split * kGroupsPerBox + kp - 1) / kp <= kPreGroups;
     return p;
   };
   if (g_override.rows) {
@@ -534,12 +583,13 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
     return p.smem <= 200 * 1024 ? p : MmaGemvPlan{};
   }
   // Measured on B200 over Qwen2-1.5B shapes (chains of 28 PDL launches,
-  // M = 1..16): 8 warps per CTA; 16-row tiles below M = 8 and 32-row tiles
-  // from there (the activation fragments are then shared by more weight rows).
+  // M = 1..16): 8 warps per CTA; 16-row tiles, except from M = 8 on for
+  // grids of more than two 16-row tiles per SM or rows of 16+ boxes, which
+  // take 32-row tiles (the activation fragments then serve more rows).
   // K stays whole for M < 4 unless shared memory runs out. From M = 4 on, rows
   // of at least 16 boxes are split over a cluster until the grid has 1.5 CTAs
   // per SM, keeping each CTA within 110 KB so that two fit on an SM.
-  const int R = M >= 8 ? 32 : 16;
+  const int R = (M >= 8 && ((N + 15) / 16 > 2 * (int64_t)num_sms || nboxes >= 16)) ? 32 : 16;
   const int64_t tiles = (N + R - 1) / R;
   // `req` is the requested split; make() may round it down to the number of
   // CTAs that get boxes, so the loops step `req`, which always terminates.
@@ -580,9 +630,9 @@ cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, co
   a.boxes_per_split = p.boxes_per_split;
   a.G = (int)(K / kGroup);
   switch (x_dtype) {
-    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
-    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
-    default: return launch_x<QI4_DTYPE_F32>(map, a, p.nt, p.warps, p.ksplit, stream, pdl);
+    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+    default: return launch_x<QI4_DTYPE_F32>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
   }
 }
 

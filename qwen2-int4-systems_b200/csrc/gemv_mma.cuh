@@ -13,6 +13,7 @@ struct MmaGemvPlan {
   int warps;            // warps per CTA: 2, 4, 8 or 16 (rows / 16 <= warps)
   int boxes_per_split;  // 128-byte (4-group) boxes of K per CTA
   int nt;               // n8 token tiles: 1 (M <= 8) or 2 (M <= 16)
+  int pre;              // 1: weight fragments expanded before the dependency wait
   size_t smem;
 };
 

@@ -80,7 +80,7 @@ def test_gemv_planner_always_terminates_with_a_valid_plan(b200):
     CTA of a K split gets at least one 128-byte box, and the plan fits the
     shared memory the kernel is configured for."""
     _, lib = _lib(b200)
-    plan = (ctypes.c_int64 * 5)()
+    plan = (ctypes.c_int64 * 6)()
     shapes = [(n, k) for n in (1, 7, 100, 256, 1000, 1536, 8960, 151936)
               for k in (64, 128, 192, 960, 1536, 4096, 8960, 64 * 141)]
     for sms in (148, 132, 8):
@@ -88,23 +88,26 @@ def test_gemv_planner_always_terminates_with_a_valid_plan(b200):
             for dtype in (0, 1, 2):
                 for n, k in shapes:
                     assert lib.qi4_gemv_mma_plan(m, n, k, dtype, sms, plan) == 0, (m, n, k, dtype)
-                    rows, ks, warps, bps, smem = list(plan)
+                    rows, ks, warps, bps, smem, pre = list(plan)
                     nboxes = (k // 64 + 3) // 4
                     assert rows in (16, 32, 64, 128) and warps in (2, 4, 8, 16) and rows // 16 <= warps
                     assert 1 <= ks <= 8 and bps * (ks - 1) < nboxes <= bps * ks, (m, n, k, ks, bps)
                     assert smem <= 200 * 1024, (m, n, k, dtype, smem)
+                    if pre:  # single wave, at most 4 groups per warp
+                        assert warps == 8 and -(-n // rows) * ks <= sms
+                        assert -(-(bps * 4) // (warps // (rows // 16))) <= 4
     assert lib.qi4_gemv_mma_plan(17, 64, 64, 1, 148, plan) == -3
     assert lib.qi4_gemv_mma_plan(1, 64, 100, 1, 148, plan) == -3
 
 
 def test_gemv_planner_honours_and_validates_overrides(b200):
     _, lib = _lib(b200)
-    plan = (ctypes.c_int64 * 5)()
+    plan = (ctypes.c_int64 * 6)()
     assert lib.qi4_gemv_mma_plan_override(32, 5, 4) == 0
     try:
         assert lib.qi4_gemv_mma_plan(1, 1000, 1536, 1, 148, plan) == 0
         # 6 boxes split 5 ways: 2 boxes per CTA, so only 3 CTAs carry work
-        assert list(plan)[:4] == [32, 3, 4, 2]
+        assert list(plan)[:4] == [32, 3, 4, 2] and plan[5] == 0
     finally:
         lib.qi4_gemv_mma_plan_override(0, 0, 0)
     for bad in ((24, 1, 4), (16, 0, 4), (16, 9, 4), (16, 1, 3), (64, 1, 2)):
