@@ -180,12 +180,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-template <int XT>
+// MULTI: also stage 2..8 chunks per thread through registers (unrolled; kept
+// out of kernels whose post-wait code should stay short).
+template <int XT, bool MULTI>
 __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride, int g0, int gs, int tid,
                                         int nthreads) {
   const int per_tok = gs * 8;  // 8-element chunks per token
   const int total = a.M * per_tok;
   const uint32_t base = smem_addr(xs);
+  constexpr int kRegChunks = 8;  // chunks per thread staged through registers
   if (XT != QI4_DTYPE_F32 && total <= nthreads) {
     // One chunk per thread at most: load, permute, store.
     if (tid < total) {
@@ -194,6 +197,28 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
                                                            (int64_t)tok * a.K + (int64_t)g0 * kGroup + c * 8));
       sts128(base + tok * xstride + c * 16,
              make_uint4(prmt_lo(v.x, v.z), prmt_hi(v.x, v.z), prmt_lo(v.y, v.w), prmt_hi(v.y, v.w)));
+    }
+  } else if (MULTI && XT != QI4_DTYPE_F32 && total <= kRegChunks * nthreads) {
+    // Up to kRegChunks chunks per thread: all loads first (one round trip),
+    // then permute and store.
+    uint4 v[kRegChunks];
+#pragma unroll
+    for (int u = 0; u < kRegChunks; ++u) {
+      const int i = tid + u * nthreads;
+      if (i < total) {
+        const int tok = a.M == 1 ? 0 : i / per_tok, c = i - tok * per_tok;
+        v[u] = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(a.x) + (int64_t)tok * a.K +
+                                                    (int64_t)g0 * kGroup + c * 8));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRegChunks; ++u) {
+      const int i = tid + u * nthreads;
+      if (i < total) {
+        const int tok = a.M == 1 ? 0 : i / per_tok, c = i - tok * per_tok;
+        sts128(base + tok * xstride + c * 16, make_uint4(prmt_lo(v[u].x, v[u].z), prmt_hi(v[u].x, v[u].z),
+                                                         prmt_lo(v[u].y, v[u].w), prmt_hi(v[u].y, v[u].w)));
+      }
     }
   } else if constexpr (XT != QI4_DTYPE_F32) {
     // Asynchronous 16-byte copies straight into place (all in flight at
@@ -393,14 +418,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
       }
     }
     pdl_wait();  // activations come from the previous kernel
-    stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
+    stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < PRE; ++j)
       if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, gq, a.M, x_lane, xstride, gs);
   } else {
     pdl_wait();  // activations come from the previous kernel
-    stage_x<XT>(a, xs, xstride, g0, gs, tid, kThr);
+    stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 
     uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
