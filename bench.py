@@ -24,6 +24,7 @@ Multi-GPU (torchrun): independent replicas, one per rank, weak scaling.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import importlib
 import json
 import os
@@ -194,6 +195,44 @@ class Chain:
 
     def flops(self) -> int:
         return sum(2 * self.m * e["n"] * e["k"] for e in self.entries)
+
+
+class GroupedChain:
+    """The decode step with the linears that share an input grouped into one
+    C-ABI launch (qi4_w4g64_linear_multi): per layer q/k/v, o, gate/up, down
+    (4 launches instead of 7). Same weights, same bytes, same outputs."""
+
+    GROUPS = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
+
+    def __init__(self, lib, layers: list[list[dict]], device, gen: torch.Generator):
+        self.lib = lib
+        self.launches = []
+        for layer in layers:
+            by_name = {e["name"]: e for e in layer}
+            for group in self.GROUPS:
+                ents = [by_name[n] for n in group]
+                k = ents[0]["k"]
+                x = torch.randn(1, k, device=device, generator=gen).to(torch.bfloat16)
+                outs = [torch.empty(1, e["n"], device=device, dtype=torch.bfloat16) for e in ents]
+                c = len(ents)
+                arr = lambda vals: (ctypes.c_void_p * c)(*vals)
+                bias = [e["bias"] for e in ents]
+                self.launches.append((x, outs, c, k, arr([e["qweight"].data_ptr() for e in ents]),
+                                      arr([e["scales"].data_ptr() for e in ents]),
+                                      arr([e["zeros"].data_ptr() for e in ents]),
+                                      arr([None if b is None else b.data_ptr() for b in bias]),
+                                      1 if any(b is not None for b in bias) else -1,
+                                      arr([o.data_ptr() for o in outs]),
+                                      (ctypes.c_int64 * c)(*[e["n"] for e in ents])))
+
+    def launch(self):
+        stream = torch.cuda.current_stream().cuda_stream
+        for x, outs, c, k, qw, sc, z, b, bd, o, ns in self.launches:
+            rc = self.lib.qi4_w4g64_linear_multi(x.data_ptr(), 1, 1, k, c, qw, sc, z, b, bd, o, ns, stream)
+            if rc:
+                raise RuntimeError(f"grouped launch failed: {rc}")
+
+    graph = Chain.graph
 
 
 def time_graph(g: torch.cuda.CUDAGraph, reps: int, warmup: int) -> float:
@@ -483,6 +522,13 @@ def main() -> None:
         per_shape[name] = {"m": 1, "us_per_launch": t * 1e3 / LAYERS,
                            "GBps": chain.bytes() / (t / 1e3) / 1e9}
     gate = per_shape["gate"]
+
+    # The same step with the input-sharing linears grouped per launch.
+    grouped = GroupedChain(lib, layers, device, gen)
+    t = time_graph(grouped.graph(), reps=20, warmup=3)
+    decode_grouped = {"launches_per_step": len(grouped.launches), "ms_per_step": t,
+                      "GBps": step_bytes / (t / 1e3) / 1e9,
+                      "api": "qi4_w4g64_linear_multi (q/k/v and gate/up grouped), CUDA graph"}
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     if peaks_path.exists():
         peaks = json.loads(peaks_path.read_text())
@@ -578,7 +624,8 @@ def main() -> None:
                    "bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
         "gpu_launches": launches_per_step * args.steps,
-        "roofline": roofline, "per_shape_m1": per_shape, "gemm_m2048": gemm, "qwen2_decode": decode,
+        "roofline": roofline, "per_shape_m1": per_shape, "decode_step_grouped": decode_grouped,
+        "gemm_m2048": gemm, "qwen2_decode": decode,
         "split_prefill_mlp": split,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))

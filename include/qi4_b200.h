@@ -125,6 +125,23 @@ QI4_API int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, c
                                          const void* bias, int bias_dtype, float* out, int64_t N,
                                          void* stream);
 
+/* Several linears that share one activation block, in one launch: for
+ * i < count (1..3), outs[i] = x @ W_i^T (+ biases[i]) with W_i given by
+ * qweights[i] / scales_f16[i] / zeros[i] (same format and rules as
+ * qi4_w4g64_linear; N = Ns[i], K common). The pointer arrays are HOST arrays
+ * of device pointers; zeros and biases may be NULL arrays or hold NULL
+ * entries; bias_dtype applies to every bias. For M <= 16 the matrices share
+ * one GEMV launch (the activations are staged once and one dependent launch
+ * replaces `count`, e.g. q/k/v or gate/up of a decoder layer); for larger M
+ * it issues one tensor-core launch per matrix. Outputs equal those of
+ * `count` separate qi4_w4g64_linear calls within the GEMV tolerance. No
+ * reference counterpart: the reference calls each QuantLinear separately
+ * (src/qwen_int4/model.py:71-73 q/k/v, model.py:134-135 gate/up). */
+QI4_API int qi4_w4g64_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                                   const uint8_t* const* qweights, const uint16_t* const* scales_f16,
+                                   const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                   void* const* outs, const int64_t* Ns, void* stream);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
  * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8 or 16,

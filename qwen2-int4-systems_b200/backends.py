@@ -22,6 +22,8 @@ the caller's current CUDA stream; nothing here computes on the CPU.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -165,6 +167,49 @@ def b200_w4g64_linear(
     if x2.shape[0]:
         _launch_linear(_aligned(x2), qweight, scales, zeros, bias, out, out_features, algo, pdl)
     return out.reshape(*x.shape[:-1], out_features)
+
+
+def b200_w4g64_linear_multi(x: torch.Tensor, layers) -> list[torch.Tensor]:
+    """Several canonical W4G64 linears that share the activations ``x`` (for
+    example a decoder layer's q/k/v or gate/up projections), in one launch for
+    decode sizes. ``layers`` holds one to three objects with the QuantLinear
+    buffers and sizes (``qweight``, ``scales``, ``zeros``, ``bias``,
+    ``in_features``, ``out_features``). Returns one output per layer, each as
+    ``b200_w4g64_linear`` would (same dtype, shape and tolerance). No reference
+    counterpart: the reference runs each QuantLinear separately.
+    """
+    layers = list(layers)
+    if not 1 <= len(layers) <= 3:
+        raise ValueError("b200_w4g64_linear_multi takes one to three layers")
+    k = layers[0].in_features
+    biases = [getattr(l, "bias", None) for l in layers]
+    if any(l.in_features != k for l in layers):
+        raise ValueError("grouped linears must share in_features")
+    if len({b.dtype for b in biases if b is not None}) > 1:
+        raise TypeError("grouped linears must share one bias dtype")
+    for l, b in zip(layers, biases):
+        _validate_linear(x, l.qweight, l.scales, l.zeros, b, l.out_features, k, GROUP_SIZE, "canonical")
+    lib = _require_cuda()
+    x2 = _aligned(x.reshape(-1, k))
+    outs = [torch.empty((x2.shape[0], l.out_features), dtype=x.dtype, device=x.device) for l in layers]
+    if x2.shape[0]:
+        device = x2.device
+        if torch.cuda.current_device() != device.index:
+            with torch.cuda.device(device):
+                return b200_w4g64_linear_multi(x, layers)
+        if any(l.qweight.data_ptr() % 16 for l in layers):
+            raise ValueError("qweight storage must be 16-byte aligned for the B200 kernels")
+        n = len(layers)
+        arr = lambda vals: (ctypes.c_void_p * n)(*vals)
+        bias_dtype = next((_DTYPE_CODE[b.dtype] for b in biases if b is not None), _lib.DTYPE_NONE)
+        rc = lib.qi4_w4g64_linear_multi(
+            x2.data_ptr(), _DTYPE_CODE[x2.dtype], x2.shape[0], k, n,
+            arr([l.qweight.data_ptr() for l in layers]), arr([l.scales.data_ptr() for l in layers]),
+            arr([l.zeros.data_ptr() for l in layers]), arr([_ptr(b) for b in biases]), bias_dtype,
+            arr([o.data_ptr() for o in outs]), (ctypes.c_int64 * n)(*[l.out_features for l in layers]),
+            _stream(device))
+        _lib.check(rc, "qi4_w4g64_linear_multi")
+    return [o.reshape(*x.shape[:-1], l.out_features) for o, l in zip(outs, layers)]
 
 
 def linear_canonical_w4g64_b200(

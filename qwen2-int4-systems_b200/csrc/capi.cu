@@ -197,11 +197,67 @@ static int linear_impl(const void* x, int x_dtype, int64_t M, int64_t K, const u
   return QI4_OK;
 }
 
+static int linear_multi_impl(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                             const uint8_t* const* qweights, const uint16_t* const* scales,
+                             const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                             void* const* outs, const int64_t* Ns, void* stream_ptr) {
+  clear_error();
+  if (count < 1 || count > 3 || !qweights || !scales || !outs || !Ns) {
+    set_error("count must be 1..3 and qweights, scales, outs, Ns non-null host arrays");
+    return QI4_ERR_ARGUMENT;
+  }
+  bool any_bias = false;
+  for (int i = 0; i < count; ++i) {
+    const void* b = biases ? biases[i] : nullptr;
+    any_bias |= b != nullptr;
+    const int rc = validate_linear(x, x_dtype, M, K, qweights[i], scales[i], b, bias_dtype, outs[i], Ns[i]);
+    if (rc) return rc;
+  }
+  if (!any_bias) bias_dtype = QI4_DTYPE_NONE;
+  if (M > kGemvMaxM) {
+    // Prefill sizes: one tensor-core launch per matrix.
+    for (int i = 0; i < count; ++i) {
+      const int rc = linear_impl(x, x_dtype, M, K, qweights[i], scales[i], zeros ? zeros[i] : nullptr,
+                                 biases ? biases[i] : nullptr, bias_dtype, outs[i], Ns[i], stream_ptr,
+                                 QI4_ALGO_AUTO, 1);
+      if (rc) return rc;
+    }
+    return QI4_OK;
+  }
+  DeviceInfo info;
+  int rc = current_device(info);
+  if (rc) return rc;
+  const uint8_t* zs[3] = {nullptr, nullptr, nullptr};
+  const void* bs[3] = {nullptr, nullptr, nullptr};
+  int64_t n_eff = 0;
+  for (int i = 0; i < count; ++i) {
+    zs[i] = zeros ? zeros[i] : nullptr;
+    bs[i] = biases ? biases[i] : nullptr;
+    n_eff += (Ns[i] + 15) / 16 * 16;
+  }
+  const MmaGemvPlan plan = plan_gemv_mma(M, n_eff, K, x_dtype, info.sms);
+  if (plan.rows == 0) {
+    set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)n_eff, (long long)K);
+    return QI4_ERR_SHAPE;
+  }
+  return check_launch(launch_gemv_mma_multi(x, x_dtype, M, K, count, qweights, scales, zs, bs, bias_dtype, outs, Ns,
+                                            static_cast<cudaStream_t>(stream_ptr), true, plan),
+                      "w4g64 grouped GEMV");
+}
+
 }  // namespace qi4
 
 using namespace qi4;
 
 extern "C" {
+
+int qi4_w4g64_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                           const uint8_t* const* qweights, const uint16_t* const* scales_f16,
+                           const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                           void* const* outs, const int64_t* Ns, void* stream) {
+  return linear_multi_impl(x, x_dtype, M, K, count, qweights, scales_f16, zeros, biases, bias_dtype, outs, Ns,
+                           stream);
+}
 
 int qi4_w4g64_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
                      const uint16_t* scales_f16, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,

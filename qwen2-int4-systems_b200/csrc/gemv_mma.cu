@@ -50,17 +50,25 @@ constexpr int kBoxBytes = 128;  // inner TMA box: 128 bytes = 256 codes = 4 grou
 constexpr int kGroupsPerBox = 4;
 constexpr int kPreGroups = 4;  // groups per warp expanded before the dependency wait
 
+constexpr int kMaxMats = 3;  // weight matrices sharing one activation block per launch
+
+// One weight matrix of a launch (several share the activations: q/k/v, gate/up).
+struct Mat {
+  const __half* scales;
+  const uint8_t* zeros;
+  const void* bias;
+  void* out;
+  int64_t N;
+};
+
 struct Args {
   const void* x;
   int M;
   int64_t K;
-  const __half* scales;
-  const uint8_t* zeros;
-  const void* bias;
+  Mat mat[kMaxMats];
+  int tiles_end[kMaxMats];  // cumulative row tiles: matrix m owns tiles [tiles_end[m-1], tiles_end[m])
+  int nmats;
   int bias_dtype;
-  void* out;
-  int out_dtype;
-  int64_t N;
   int rows;             // R
   int rows_log2;
   int boxes_per_split;  // boxes along K per CTA
@@ -265,7 +273,7 @@ __host__ __device__ constexpr int x_stride_bytes(int bps, bool f32) { return bps
 // and zero points of four consecutive groups of a row are one 8-byte and one
 // 2-byte load when the row length in groups is a multiple of four.
 template <int XT>
-__device__ __forceinline__ void build_table(const Args& a, TableEntry* table, int tstride, int64_t row0, int g0,
+__device__ __forceinline__ void build_table(const Args& a, const Mat& mt, TableEntry* table, int tstride, int64_t row0, int g0,
                                             int gs, int tid, int nthreads) {
   const int R = a.rows;
   const int nch = (gs + 3) >> 2;
@@ -275,20 +283,20 @@ __device__ __forceinline__ void build_table(const Args& a, TableEntry* table, in
     const int64_t row = row0 + r;
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t znib = 0;  // the four groups' stored zero nibbles (two's complement; 0 when absent)
-    if (row < a.N) {
+    if (row < mt.N) {
       const int64_t gi = row * a.G + g0 + g;
       if (vec && g + 4 <= gs) {
-        const uint2 sv = __ldg(reinterpret_cast<const uint2*>(a.scales + gi));
+        const uint2 sv = __ldg(reinterpret_cast<const uint2*>(mt.scales + gi));
         const float2 s01 = __half22float2(*reinterpret_cast<const __half2*>(&sv.x));
         const float2 s23 = __half22float2(*reinterpret_cast<const __half2*>(&sv.y));
         s[0] = s01.x; s[1] = s01.y; s[2] = s23.x; s[3] = s23.y;
-        if (a.zeros) znib = __ldg(reinterpret_cast<const unsigned short*>(a.zeros + (gi >> 1)));
+        if (mt.zeros) znib = __ldg(reinterpret_cast<const unsigned short*>(mt.zeros + (gi >> 1)));
       } else {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (g + j < gs) {
-            s[j] = __half2float(__ldg(a.scales + gi + j));
-            if (a.zeros) znib |= (uint32_t)((__ldg(a.zeros + ((gi + j) >> 1)) >> (((gi + j) & 1) * 4)) & 0xF) << (4 * j);
+            s[j] = __half2float(__ldg(mt.scales + gi + j));
+            if (mt.zeros) znib |= (uint32_t)((__ldg(mt.zeros + ((gi + j) >> 1)) >> (((gi + j) & 1) * 4)) & 0xF) << (4 * j);
           }
         }
       }
@@ -299,6 +307,17 @@ __device__ __forceinline__ void build_table(const Args& a, TableEntry* table, in
       if (g + j < gs)
         t[j] = TableEntry{s[j], Fmt<XT>::kMagic + (((znib >> (4 * j)) & 0xF) ^ 0x8u) * 0x00010001u};
   }
+}
+
+// The output has the activations' dtype (FP32 for FP32 activations).
+template <int XT>
+__device__ __forceinline__ void store_out(void* out, int64_t i, float v) {
+  if constexpr (XT == QI4_DTYPE_F32)
+    static_cast<float*>(out)[i] = v;
+  else if constexpr (XT == QI4_DTYPE_BF16)
+    static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half*>(out)[i] = __float2half_rn(v);
 }
 
 // D = (c - z) . x for one group of 64 k and the lane's token tile(s), then
@@ -337,7 +356,8 @@ __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* a
 }
 
 template <int XT, int NT, int WARPS, int PRE>
-__global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap, const Args a) {
+__global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
+                const __grid_constant__ CUtensorMap wmap2, const Args a) {
   // PRE > 0: every warp has at most PRE groups, expanded into registers
   // before the dependency wait (single-wave grids, whose CTAs start early).
   constexpr int kThr = WARPS * 32;
@@ -352,7 +372,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
   const int nbox = max(0, min(a.boxes_per_split, nbox_total - box0));  // 0 only for a CTA past the end
   const int g0 = box0 * kGroupsPerBox;
   const int gs = max(0, min(a.G - g0, nbox * kGroupsPerBox));  // groups of this CTA
-  const int64_t row0 = (int64_t)blockIdx.x * R;
+  // The CTA's matrix and its row tile within that matrix.
+  const int tile = blockIdx.x;
+  const int m = (a.nmats > 1 && tile >= a.tiles_end[0]) + (a.nmats > 2 && tile >= a.tiles_end[1]);
+  const Mat& mt = m == 0 ? a.mat[0] : (m == 1 ? a.mat[1] : a.mat[2]);
+  const CUtensorMap* wmap = m == 0 ? &wmap0 : (m == 1 ? &wmap1 : &wmap2);
+  const int64_t row0 = (int64_t)(tile - (m == 0 ? 0 : a.tiles_end[m - 1])) * R;
 
   const int tstride = a.boxes_per_split * kGroupsPerBox + 1;  // odd stride: conflict-free table reads
   uint8_t* wsm = smem;                                         // nbox x R x 128
@@ -371,10 +396,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
     fence_barrier_init();
     for (int b = 0; b < nbox; ++b) {
       mbar_arrive_expect_tx(bars + b, (uint32_t)(R * kBoxBytes));
-      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, &wmap, (box0 + b) * kBoxBytes, (int)row0, bars + b);
+      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, wmap, (box0 + b) * kBoxBytes, (int)row0, bars + b);
     }
   }
-  build_table<XT>(a, table, tstride, row0, g0, gs, tid, kThr);
+  build_table<XT>(a, mt, table, tstride, row0, g0, gs, tid, kThr);
   __syncthreads();  // barriers initialised, table complete
 
   const int warp = tid >> 5, lane = tid & 31;
@@ -467,7 +492,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
   __syncthreads();
   const bool split = gridDim.y > 1;
   for (int i = tid; i < R * a.M; i += kThr) {
-    const int tok = i / R, r = i - tok * R;
+    const int tok = i >> a.rows_log2, r = i - (tok << a.rows_log2);
     float sum = 0.f;
 #pragma unroll
     for (int q = 0; q < WARPS; ++q)  // KP <= WARPS
@@ -476,9 +501,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
       part[(size_t)r * ld + tok] = sum;
     } else {
       const int64_t row = row0 + r;
-      if (row < a.N) {
-        const float bv = a.bias ? load_as_f32(a.bias, a.bias_dtype, row) : 0.f;
-        store_from_f32(a.out, a.out_dtype, (int64_t)tok * a.N + row, sum + bv);
+      if (row < mt.N) {
+        const float bv = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, row) : 0.f;
+        store_out<XT>(mt.out, (int64_t)tok * mt.N + row, sum + bv);
       }
     }
   }
@@ -497,11 +522,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
     for (int i = lo + tid; i < hi; i += kThr) {
       const int r = i / (NT * 8), tok = i - r * (NT * 8);
       const int64_t row = row0 + r;
-      if (tok >= a.M || row >= a.N) continue;
+      if (tok >= a.M || row >= mt.N) continue;
       float sum = 0.f;
       for (int q = 0; q < nranks; ++q) sum += cluster.map_shared_rank(part, q)[i];
-      const float b = a.bias ? load_as_f32(a.bias, a.bias_dtype, row) : 0.f;
-      store_from_f32(a.out, a.out_dtype, (int64_t)tok * a.N + row, sum + b);
+      const float b = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, row) : 0.f;
+      store_out<XT>(mt.out, (int64_t)tok * mt.N + row, sum + b);
     }
   }
   cluster.sync();
@@ -517,7 +542,7 @@ size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32) {
 }
 
 template <int XT, int NT, int WARPS, int PRE>
-cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
+cudaError_t launch_t(const CUtensorMap* maps, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
   auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE>;
   static unsigned long long configured = 0;
   int dev = 0;
@@ -531,7 +556,7 @@ cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStre
     configured |= bit;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.N + a.rows - 1) / a.rows), (unsigned)ksplit, 1);
+  cfg.gridDim = dim3((unsigned)a.tiles_end[a.nmats - 1], (unsigned)ksplit, 1);
   cfg.blockDim = dim3(WARPS * 32, 1, 1);
   cfg.dynamicSmemBytes = smem_bytes(a.rows, WARPS, a.boxes_per_split, NT, a.M, XT == QI4_DTYPE_F32);
   cfg.stream = stream;
@@ -549,11 +574,11 @@ cudaError_t launch_t(const CUtensorMap& map, const Args& a, int ksplit, cudaStre
   }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, map, a);
+  return cudaLaunchKernelEx(&cfg, kernel, maps[0], maps[1], maps[2], a);
 }
 
 template <int XT, int NT>
-cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int ksplit, int pre, cudaStream_t s,
+cudaError_t launch_w(const CUtensorMap* map, const Args& a, int warps, int ksplit, int pre, cudaStream_t s,
                      bool pdl) {
   switch (warps) {
     case 2: return launch_t<XT, NT, 2, 0>(map, a, ksplit, s, pdl);
@@ -564,7 +589,7 @@ cudaError_t launch_w(const CUtensorMap& map, const Args& a, int warps, int kspli
 }
 
 template <int XT>
-cudaError_t launch_x(const CUtensorMap& map, const Args& a, int nt, int warps, int ksplit, int pre,
+cudaError_t launch_x(const CUtensorMap* map, const Args& a, int nt, int warps, int ksplit, int pre,
                      cudaStream_t s, bool pdl) {
   return nt <= 1 ? launch_w<XT, 1>(map, a, warps, ksplit, pre, s, pdl)
                  : launch_w<XT, 2>(map, a, warps, ksplit, pre, s, pdl);
@@ -632,33 +657,54 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
 
 bool gemv_mma_supported(int64_t M, int64_t K) { return M >= 1 && M <= 16 && K % kGroup == 0; }
 
-cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
-                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
-                            void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& p) {
-  CUtensorMap map;
-  if (!tensor_map_2d(&map, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
-                     (uint64_t)(K / 2), kBoxBytes, (uint32_t)p.rows, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
-  Args a;
+cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                                  const uint8_t* const* qweights, const uint16_t* const* scales,
+                                  const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                  void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl,
+                                  const MmaGemvPlan& p) {
+  if (count < 1 || count > kMaxMats) return cudaErrorInvalidValue;
+  CUtensorMap maps[kMaxMats];
+  Args a{};
   a.x = x;
   a.M = (int)M;
   a.K = K;
-  a.scales = reinterpret_cast<const __half*>(scales);
-  a.zeros = zeros;
-  a.bias = bias;
+  a.nmats = count;
   a.bias_dtype = bias_dtype;
-  a.out = out;
-  a.out_dtype = x_dtype;
-  a.N = N;
   a.rows = p.rows;
   a.rows_log2 = __builtin_ctz((unsigned)p.rows);
   a.boxes_per_split = p.boxes_per_split;
   a.G = (int)(K / kGroup);
-  switch (x_dtype) {
-    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
-    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
-    default: return launch_x<QI4_DTYPE_F32>(map, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+  int64_t tiles = 0;
+  for (int i = 0; i < kMaxMats; ++i) {
+    const int j = i < count ? i : count - 1;  // unused slots repeat the last matrix
+    if (i < count) {
+      if (!tensor_map_2d(&maps[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)Ns[i],
+                         (uint64_t)(K / 2), kBoxBytes, (uint32_t)p.rows, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+      tiles += (Ns[i] + p.rows - 1) / p.rows;
+    } else {
+      maps[i] = maps[j];
+    }
+    a.mat[i].scales = reinterpret_cast<const __half*>(scales[j]);
+    a.mat[i].zeros = zeros[j];
+    a.mat[i].bias = biases ? biases[j] : nullptr;
+    a.mat[i].out = outs[j];
+    a.mat[i].N = Ns[j];
+    if (tiles > INT32_MAX / 2) return cudaErrorInvalidValue;
+    a.tiles_end[i] = (int)tiles;
   }
+  switch (x_dtype) {
+    case QI4_DTYPE_F16: return launch_x<QI4_DTYPE_F16>(maps, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+    case QI4_DTYPE_BF16: return launch_x<QI4_DTYPE_BF16>(maps, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+    default: return launch_x<QI4_DTYPE_F32>(maps, a, p.nt, p.warps, p.ksplit, p.pre, stream, pdl);
+  }
+}
+
+cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
+                            void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& p) {
+  return launch_gemv_mma_multi(x, x_dtype, M, K, 1, &qweight, &scales, &zeros, &bias, bias_dtype, &out, &N, stream,
+                               pdl, p);
 }
 
 int read_gemv_mma_error(cudaStream_t stream) {

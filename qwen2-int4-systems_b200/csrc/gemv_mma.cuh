@@ -23,6 +23,14 @@ void set_gemv_mma_override(int rows, int ksplit, int warps);  // rows = 0 restor
 cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
                             const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
                             void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& plan);
+// One launch over `count` (1..3) weight matrices that share the activations x
+// (q/k/v, gate/up): matrix i writes outs[i] (M x Ns[i]); biases may be null.
+// The plan is that of an N of sum(round_up(Ns[i], 16)).
+cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                                  const uint8_t* const* qweights, const uint16_t* const* scales,
+                                  const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                  void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl,
+                                  const MmaGemvPlan& plan);
 // Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
 int read_gemv_mma_error(cudaStream_t stream);
 

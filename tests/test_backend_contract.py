@@ -163,3 +163,20 @@ def test_register_with_reference_adds_explicit_backend(b200):
     finally:
         for key in [k for k in sys.modules if k.startswith(name)]:
             del sys.modules[key]
+
+
+def test_grouped_linear_rejects_bad_groups_without_a_gpu(b200):
+    from types import SimpleNamespace
+
+    qw, sc, z = _tensors(64, 128)
+    lay = SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=128, out_features=64)
+    other = SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=192, out_features=64)
+    x = torch.ones(1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="one to three"):
+        b200.b200_w4g64_linear_multi(x, [])
+    with pytest.raises(ValueError, match="one to three"):
+        b200.b200_w4g64_linear_multi(x, [lay] * 4)
+    with pytest.raises(ValueError, match="share in_features"):
+        b200.b200_w4g64_linear_multi(x, [lay, other])
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        b200.b200_w4g64_linear_multi(x, [lay, lay])
