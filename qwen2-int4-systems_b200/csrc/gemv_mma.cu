@@ -320,6 +320,15 @@ __device__ __forceinline__ void store_out(void* out, int64_t i, float v) {
     static_cast<__half*>(out)[i] = __float2half_rn(v);
 }
 
+// One warp waits for the prerequisite grid (griddepcontrol.wait makes its
+// memory visible to the whole grid); the other warps sleep on the CTA barrier
+// instead of waiting themselves, so that a CTA resident ahead of its turn
+// issues nothing while the previous kernel still computes on the same SM.
+__device__ __forceinline__ void wait_prerequisites(int tid) {
+  if (tid < 32) pdl_wait();
+  __syncthreads();
+}
+
 // D = (c - z) . x for one group of 64 k and the lane's token tile(s), then
 // acc += scale * D (rows r and r + 8 of the lane; FP32 activations as two
 // MMAs of the bf16 hi and lo planes).
@@ -442,31 +451,29 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
         fs[j][1] = eh.scale;
       }
     }
-    pdl_wait();  // activations come from the previous kernel
+    wait_prerequisites(tid);  // activations come from the previous kernel
     stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < PRE; ++j)
       if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, gq, a.M, x_lane, xstride, gs);
   } else {
-    pdl_wait();  // activations come from the previous kernel
+    wait_prerequisites(tid);  // activations come from the previous kernel
     stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 
-    uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) coff[j] = (uint32_t)((((j << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
-    for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
-      // Each box has its own barrier: the first groups are used while later
-      // boxes are still in flight.
-      mbar_wait(bars + b, 0, &g_gemv_mma_error);
-      const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int g = 4 * b + j;
-        if (g < gb || g >= ge) continue;
-        const uint2 wl = lds64(box + coff[j]);
-        const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
+    if (KP % 4 == 0 && gs <= 4 * KP) {
+      // At most four groups per warp, interleaved over the KP warps of a row
+      // block (warp kp takes g = kp, kp + KP, ...): when the last box lands, each warp has at most
+      // one of its groups left, instead of one warp owning the whole box. All
+      // of a warp's groups sit at position kp % 4 of their box, so its
+      // swizzled chunk offset is fixed.
+      const uint32_t coff = (uint32_t)(((((kp & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
+      for (int g = kp; g < gs; g += KP) {
+        mbar_wait(bars + (g >> 2), 0, &g_gemv_mma_error);
+        const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes) + coff;
+        const uint2 wl = lds64(ap);
+        const uint2 wh = lds64(ap + 8 * kBoxBytes);
         const TableEntry el = t_lo[g], eh = t_hi[g];
         uint32_t al[8], ah[8];
         expand_word<XT>(wl.x, el.zc2, al);
@@ -475,8 +482,32 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_co
         expand_word<XT>(wh.y, eh.zc2, ah + 4);
         mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, gq, a.M, x_lane, xstride, gs);
       }
+    } else {
+      uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) coff[j] = (uint32_t)((((j << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
+      for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
+        // Each box has its own barrier: the first groups are used while later
+        // boxes are still in flight.
+        mbar_wait(bars + b, 0, &g_gemv_mma_error);
+        const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int g = 4 * b + j;
+          if (g < gb || g >= ge) continue;
+          const uint2 wl = lds64(box + coff[j]);
+          const uint2 wh = lds64(box + coff[j] + 8 * kBoxBytes);
+          const TableEntry el = t_lo[g], eh = t_hi[g];
+          uint32_t al[8], ah[8];
+          expand_word<XT>(wl.x, el.zc2, al);
+          expand_word<XT>(wl.y, el.zc2, al + 4);
+          expand_word<XT>(wh.x, eh.zc2, ah);
+          expand_word<XT>(wh.y, eh.zc2, ah + 4);
+          mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, gq, a.M, x_lane, xstride, gs);
+        }
+      }
     }
-  }
+    }
 
   // Every warp leaves its partial sums in shared memory ([kp][row][token]);
   // then one thread per (row, token) adds the KP partials (independent loads,
