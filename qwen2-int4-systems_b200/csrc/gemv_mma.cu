@@ -365,7 +365,7 @@ __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* a
 }
 
 template <int XT, int NT, int WARPS, int PRE>
-__global__ void __launch_bounds__(WARPS * 32, 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
+__global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const Args a) {
   // PRE > 0: every warp has at most PRE groups, expanded into registers
   // before the dependency wait (single-wave grids, whose CTAs start early).
@@ -663,10 +663,11 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
     MmaGemvPlan p = make(g_override.rows, std::min(g_override.ksplit, nboxes), w);
     return p.smem <= 200 * 1024 ? p : MmaGemvPlan{};
   }
-  // Measured on B200 over Qwen2-1.5B shapes (chains of 28 PDL launches,
-  // M = 1..16): 8 warps per CTA; 16-row tiles, except from M = 8 on for
-  // grids of more than two 16-row tiles per SM or rows of 16+ boxes, which
-  // take 32-row tiles (the activation fragments then serve more rows).
+  // Measured on B200 over Qwen2-1.5B shapes (chains of 28 PDL launches and
+  // the mixed 196-launch step, M = 1..16): 8 warps per CTA (16 for long rows,
+  // below); 16-row tiles, except from M = 8 on for grids of more than two
+  // 16-row tiles per SM or rows of 16+ boxes, which take 32-row tiles (the
+  // activation fragments then serve more rows).
   // K stays whole for M < 4 unless shared memory runs out. From M = 4 on, rows
   // of at least 16 boxes are split over a cluster until the grid has 1.5 CTAs
   // per SM, keeping each CTA within 110 KB so that two fit on an SM.
@@ -682,6 +683,14 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
       best = make(R, ++req, 8);
   }
   while (best.smem > 200 * 1024 && req < 8 && req < nboxes) best = make(R, ++req, 8);
+  // A single-wave grid with K whole whose warps would each own more than 8
+  // groups (long rows such as down_proj at M = 1) runs 16 warps per CTA
+  // (64 registers, so two CTAs still fit an SM).
+  const int kp8 = 8 / (R / 16);
+  if (best.ksplit == 1 && tiles <= num_sms && (best.boxes_per_split * kGroupsPerBox + kp8 - 1) / kp8 > 8) {
+    const MmaGemvPlan wide = make(R, 1, 16);
+    if (wide.smem <= 200 * 1024) best = wide;
+  }
   if (best.smem > 200 * 1024) best = MmaGemvPlan{};
   return best;
 }
