@@ -72,6 +72,8 @@ struct Args {
   int rows;             // R
   int rows_log2;
   int boxes_per_split;  // boxes along K per CTA
+  int copy_log2;        // log2 of the 128-byte boxes fetched per TMA copy
+  int three_d;          // 1: 3-D box-major copies (rows of K/2 bytes a multiple of 128); 0: 2-D, one box each
   int G;                // groups per row (K / 64)
 };
 
@@ -266,6 +268,20 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
   }
 }
 
+__host__ __device__ constexpr int alloc_boxes(int bps, int copy_log2) {
+  return ((bps + (1 << copy_log2) - 1) >> copy_log2) << copy_log2;
+}
+
+#ifndef QI4_GEMV_COPY_MAX
+#define QI4_GEMV_COPY_MAX 8
+#endif
+inline int copy_log2_for(int bps) {
+  if (bps > QI4_GEMV_COPY_MAX) return 2;
+  int l = 0;
+  while ((1 << l) < bps) ++l;
+  return l;
+}
+
 __host__ __device__ constexpr int x_stride_bytes(int bps, bool f32) { return bps * kGroupsPerBox * 128 * (f32 ? 2 : 1) + 16; }
 
 // Scale / zero-point table of the CTA's slab, built before the dependency
@@ -389,8 +405,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   const int64_t row0 = (int64_t)(tile - (m == 0 ? 0 : a.tiles_end[m - 1])) * R;
 
   const int tstride = a.boxes_per_split * kGroupsPerBox + 1;  // odd stride: conflict-free table reads
-  uint8_t* wsm = smem;                                         // nbox x R x 128
-  TableEntry* table = reinterpret_cast<TableEntry*>(wsm + (size_t)a.boxes_per_split * R * kBoxBytes);
+  const int copies = (nbox + (1 << a.copy_log2) - 1) >> a.copy_log2;
+  uint8_t* wsm = smem;  // boxes x R x 128, box-major (rounded up to whole copies)
+  TableEntry* table = reinterpret_cast<TableEntry*>(wsm + (size_t)alloc_boxes(a.boxes_per_split, a.copy_log2) * R * kBoxBytes);
   float* red = reinterpret_cast<float*>(table + (size_t)R * tstride);
   uint8_t* xs = reinterpret_cast<uint8_t*>(red + (size_t)(KP - 1) * RB * 32 * NT * 4 + (size_t)R * NT * 8);
   const int xstride = x_stride_bytes(a.boxes_per_split, XT == QI4_DTYPE_F32);
@@ -401,11 +418,17 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   pdl_launch_dependents();
   const int tid = threadIdx.x;
   if (tid == 0 && nbox > 0) {
-    for (int b = 0; b < nbox; ++b) mbar_init(bars + b, 1);
+    // One 3-D copy brings (1 << copy_log2) boxes of the R rows, box-major;
+    // boxes past the end of a row arrive zero-filled (and are never read).
+    for (int c = 0; c < copies; ++c) mbar_init(bars + c, 1);
     fence_barrier_init();
-    for (int b = 0; b < nbox; ++b) {
-      mbar_arrive_expect_tx(bars + b, (uint32_t)(R * kBoxBytes));
-      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, wmap, (box0 + b) * kBoxBytes, (int)row0, bars + b);
+    const int cb = 1 << a.copy_log2;
+    for (int c = 0; c < copies; ++c) {
+      mbar_arrive_expect_tx(bars + c, (uint32_t)(cb * R * kBoxBytes));
+      if (a.three_d)
+        tma_load_3d(wsm + (size_t)c * cb * R * kBoxBytes, wmap, 0, (int)row0, box0 + c * cb, bars + c);
+      else  // cb == 1
+        tma_load_2d(wsm + (size_t)c * R * kBoxBytes, wmap, (box0 + c) * kBoxBytes, (int)row0, bars + c);
     }
   }
   build_table<XT>(a, mt, table, tstride, row0, g0, gs, tid, kThr);
@@ -437,7 +460,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
     for (int j = 0; j < PRE; ++j) {
       const int g = gb + j;
       if (g < ge) {
-        mbar_wait(bars + (g >> 2), 0, &g_gemv_mma_error);
+        mbar_wait(bars + ((g >> 2) >> a.copy_log2), 0, &g_gemv_mma_error);
         const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes) +
                             (uint32_t)(((((g & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
         const uint2 wl = lds64(ap);
@@ -470,7 +493,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
       // swizzled chunk offset is fixed.
       const uint32_t coff = (uint32_t)(((((kp & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
       for (int g = kp; g < gs; g += KP) {
-        mbar_wait(bars + (g >> 2), 0, &g_gemv_mma_error);
+        mbar_wait(bars + ((g >> 2) >> a.copy_log2), 0, &g_gemv_mma_error);
         const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes) + coff;
         const uint2 wl = lds64(ap);
         const uint2 wh = lds64(ap + 8 * kBoxBytes);
@@ -489,7 +512,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
       for (int b = gb >> 2; b < (ge + 3) >> 2; ++b) {
         // Each box has its own barrier: the first groups are used while later
         // boxes are still in flight.
-        mbar_wait(bars + b, 0, &g_gemv_mma_error);
+        mbar_wait(bars + (b >> a.copy_log2), 0, &g_gemv_mma_error);
         const uint32_t box = a_row + (uint32_t)(b * R * kBoxBytes);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -563,13 +586,13 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   cluster.sync();
 }
 
-size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32) {
+size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32, int copy_log2) {
   const int RB = R / 16;
   const int KP = warps / RB > 0 ? warps / RB : 1;
   const size_t table = (size_t)R * (bps * kGroupsPerBox + 1) * sizeof(TableEntry);
   const size_t red = ((size_t)(KP - 1) * RB * 32 * NT * 4 + (size_t)R * NT * 8) * sizeof(float);
   const size_t xs = (size_t)M * x_stride_bytes(bps, f32);
-  return 1024 + (size_t)bps * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
+  return 1024 + (size_t)alloc_boxes(bps, copy_log2) * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
 }
 
 template <int XT, int NT, int WARPS, int PRE>
@@ -589,7 +612,7 @@ cudaError_t launch_t(const CUtensorMap* maps, const Args& a, int ksplit, cudaStr
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)a.tiles_end[a.nmats - 1], (unsigned)ksplit, 1);
   cfg.blockDim = dim3(WARPS * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem_bytes(a.rows, WARPS, a.boxes_per_split, NT, a.M, XT == QI4_DTYPE_F32);
+  cfg.dynamicSmemBytes = smem_bytes(a.rows, WARPS, a.boxes_per_split, NT, a.M, XT == QI4_DTYPE_F32, a.copy_log2);
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int n = 0;
@@ -648,7 +671,13 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
     p.boxes_per_split = (nboxes + ks - 1) / ks;
     p.ksplit = (nboxes + p.boxes_per_split - 1) / p.boxes_per_split;  // every CTA gets at least one box
     p.nt = nt;
-    p.smem = smem_bytes(R, warps, p.boxes_per_split, nt, (int)M, x_dtype == QI4_DTYPE_F32);
+    // Boxes per TMA copy: the whole slab in one copy up to 8 boxes (fewer,
+    // larger copies stream faster), else copies of 4 boxes so that the
+    // first groups are used while later copies are in flight.
+    // (3-D copies need rows of whole 128-byte boxes: K a multiple of 256.)
+    p.three_d = K % 256 == 0;
+    p.copy_log2 = p.three_d ? copy_log2_for(p.boxes_per_split) : 0;
+    p.smem = smem_bytes(R, warps, p.boxes_per_split, nt, (int)M, x_dtype == QI4_DTYPE_F32, p.copy_log2);
     // A single-wave grid (one CTA per SM at most) starts ahead of the
     // previous kernel's end; with at most kPreGroups groups per warp its
     // weight fragments are expanded before the dependency wait.
@@ -713,14 +742,19 @@ cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t
   a.rows = p.rows;
   a.rows_log2 = __builtin_ctz((unsigned)p.rows);
   a.boxes_per_split = p.boxes_per_split;
+  a.copy_log2 = p.copy_log2;
+  a.three_d = p.three_d;
   a.G = (int)(K / kGroup);
   int64_t tiles = 0;
   for (int i = 0; i < kMaxMats; ++i) {
     const int j = i < count ? i : count - 1;  // unused slots repeat the last matrix
     if (i < count) {
-      if (!tensor_map_2d(&maps[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)Ns[i],
-                         (uint64_t)(K / 2), kBoxBytes, (uint32_t)p.rows, CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
+      const bool ok = p.three_d ? tensor_map_row_boxes(&maps[i], qweights[i], (uint64_t)(K / 2), (uint64_t)Ns[i],
+                                                       (uint32_t)p.rows, 1u << p.copy_log2)
+                                : tensor_map_2d(&maps[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2),
+                                                (uint64_t)Ns[i], (uint64_t)(K / 2), kBoxBytes, (uint32_t)p.rows,
+                                                CU_TENSOR_MAP_SWIZZLE_128B);
+      if (!ok) return cudaErrorInvalidValue;
       tiles += (Ns[i] + p.rows - 1) / p.rows;
     } else {
       maps[i] = maps[j];

@@ -14,6 +14,8 @@ struct MmaGemvPlan {
   int boxes_per_split;  // 128-byte (4-group) boxes of K per CTA
   int nt;               // n8 token tiles: 1 (M <= 8) or 2 (M <= 16)
   int pre;              // 1: weight fragments expanded before the dependency wait
+  int copy_log2;        // log2 of the 128-byte boxes per TMA copy
+  int three_d;          // 1: 3-D box-major copies (K a multiple of 256)
   size_t smem;
 };
 

@@ -24,6 +24,13 @@ namespace qi4 {
 // shape, box) and copied out; returns false on failure (error recorded).
 bool tensor_map_2d(CUtensorMap* out, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t rows,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+// A row-major byte matrix [rows][row_bytes] (row_bytes a multiple of 128) as a
+// 3-D map (128-byte box, row, box index) with 128-byte swizzle: one copy of
+// [box_rows rows x boxes_per_copy boxes] lands box-major in shared memory
+// (box b of row r at (b * box_rows + r) * 128), the layout of as many 2-D
+// [box_rows x 128 B] copies, in one request.
+bool tensor_map_row_boxes(CUtensorMap* out, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_rows,
+                          uint32_t boxes_per_copy);
 
 // Device-side error flags (one per translation unit), read and cleared on host.
 constexpr int kErrWaitTimeout = 1;
@@ -116,6 +123,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // 2-D tiled bulk tensor load global -> this CTA's shared memory, completing
 // `bytes` on `bar`. x is the inner coordinate (elements), y the row.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
