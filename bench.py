@@ -34,6 +34,7 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -418,6 +419,49 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
             "collectives": "2 x all_gather_into_tensor (NCCL) per MLP", "ranks": world}
 
 
+def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
+    """Secondary figures for the BASELINE configs the headline does not cover:
+    config 0 (gate, symmetric, M = 1/4/16), config 1's remaining M points
+    (8/32/128/512, seven shapes of four layers), config 2 (AWQ-style
+    asymmetric down_proj, M = 1/16/2048) and config 4's batch-64 decode step
+    (196 linears at M = 64). Library-chosen kernels (GEMV up to M = 16,
+    tensor cores above), CUDA graphs of C-ABI launches."""
+    q2 = importlib.import_module(PACKAGE + ".qwen2")
+    out = {}
+
+    def run(chain, reps=10):
+        t = time_graph(chain.graph(), reps=reps, warmup=3)
+        return t, chain.bytes() / (t / 1e3) / 1e9, chain.flops() / (t / 1e3) / 1e12
+
+    gates = [layer[4] for layer in layers]
+    out["cfg0_gate_sym_GBps"] = {f"m{m}": round(run(Chain(lib, gates, m, device, gen))[1], 1) for m in (1, 4, 16)}
+    sweep = {}
+    for m in (8, 32, 128, 512):
+        t, gbps, tf = run(Chain(lib, [e for layer in layers[:4] for e in layer], m, device, gen))
+        sweep[f"m{m}"] = {"GBps": round(gbps, 1), "TFLOPs": round(tf, 2), "ms_4_layers": round(t, 4)}
+    out["cfg1_seven_shapes"] = sweep
+    # Config 2: per-input-channel scaled weights, asymmetric RTN, activations divided by the channel scale.
+    chan = torch.exp(torch.empty(8960, device=device).uniform_(float(np.log(0.5)), float(np.log(2.0)), generator=gen))
+    downs = []
+    for _ in range(4):
+        w = torch.randn(1536, 8960, device=device, generator=gen) * 0.02 * chan
+        qw, sc, z = q2.quantize_asymmetric_rtn_torch(w.to(torch.bfloat16).float())
+        downs.append({"name": "down_awq", "k": 8960, "n": 1536, "qweight": qw, "scales": sc, "zeros": z, "bias": None})
+    cfg2 = {}
+    for m in (1, 16, 2048):
+        chain = Chain(lib, downs, m, device, gen)
+        chain.x = [(x.float() / chan).to(torch.bfloat16) for x in chain.x]
+        t, _, tf = run(chain)
+        nbytes = sum(alg_bytes(m, 1536, 8960, False, asym=True) for _ in downs)
+        cfg2[f"m{m}"] = {"GBps": round(nbytes / (t / 1e3) / 1e9, 1)} if m <= 16 else \
+            {"TFLOPs": round(tf, 1), "frac_of_bf16_peak": round(tf / tensor_peak, 3)}
+    out["cfg2_awq_down"] = cfg2
+    t, _, tf = run(Chain(lib, [e for layer in layers for e in layer], 64, device, gen), reps=5)
+    out["cfg4_decode_m64"] = {"ms_per_step": round(t, 3), "tokens_per_s": round(64 / (t / 1e3), 1),
+                              "TFLOPs": round(tf, 1), "note": "196 linears at M = 64 (tensor-core path), one GPU"}
+    return out
+
+
 def profile_case(kind: str) -> None:
     """Small, ncu-sized run of the dominant kernel (see --profile-case)."""
     device = torch.device("cuda", 0)
@@ -451,6 +495,8 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm", action="store_true")
     parser.add_argument("--no-model", action="store_true", help="skip the Qwen2-1.5B decode tok/s section")
+    parser.add_argument("--no-configs", action="store_true",
+                        help="skip the secondary BASELINE config figures (configs 0, 1, 2, 4)")
     parser.add_argument("--profile-case", choices=["gemv", "gemm"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
                              "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv) or M=2048 (gemm)")
@@ -542,6 +588,10 @@ def main() -> None:
                 "frac": gate["GBps"] / hbm_peak, "peak_source": peak_src,
                 "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False)}
 
+    configs = None
+    if not args.no_configs and world == 1:
+        configs = config_sweep(lib, layers, device, gen, tensor_peak)
+
     # GEMM at M=2048 (tensor-core kernel) over one layer's seven shapes.
     gemm = None
     if not args.no_gemm and world == 1:
@@ -625,7 +675,7 @@ def main() -> None:
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": roofline, "per_shape_m1": per_shape, "decode_step_grouped": decode_grouped,
-        "gemm_m2048": gemm, "qwen2_decode": decode,
+        "gemm_m2048": gemm, "configs": configs, "qwen2_decode": decode,
         "split_prefill_mlp": split,
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))

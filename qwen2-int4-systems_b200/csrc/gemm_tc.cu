@@ -25,7 +25,14 @@
 //              K-major SW128 layout (16-byte chunk j of row r at j ^ (r % 8));
 //              then, after the last MMA, the same warps are the epilogue:
 //              tcgen05.ld 32 lanes x 32 columns, + bias (FP32), cast, store.
+// Small M (fewer tiles than SMs): the grid's z dimension splits K over a
+// thread-block cluster of up to 8 CTAs, each running its share of the packed
+// boxes through the same pipeline; their FP32 partial tiles are parked in
+// shared memory and summed over distributed shared memory, each CTA finishing
+// 128 / ksplit rows of the tile (+ bias, cast, store).
 // Every mbarrier wait is bounded (tma_util.cuh); no TMA multicast is used.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -65,6 +72,8 @@ struct Args {
   int out_dtype;
   int BN;
   int tma_out;  // 1: output tile staged in shared memory and written by one TMA store
+  int ksplit;   // CTAs per cluster along K (grid z); > 1 reduces FP32 partial tiles over DSMEM
+  int bps;      // packed 128-byte boxes (4 groups) per K split
 };
 
 // ---- tcgen05 wrappers ------------------------------------------------------
@@ -193,10 +202,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = p_empty + kPStages;  // final commit -> epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
+  float* part = reinterpret_cast<float*>(tmem_slot + 4);  // [BN][128] FP32 partial tile (K split only)
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * kTileN;
   const int m0 = blockIdx.y * BN;
-  const int KT = (int)(a.K / kGroup);  // pipeline steps (one group each)
+  // This CTA's K range: boxes [box0, box0 + bps) of the row (4 groups each).
+  const int KT_all = (int)(a.K / kGroup);
+  const int box0 = blockIdx.z * a.bps;
+  const int kb = box0 * 4;                                 // first group
+  const int KT = max(0, min(KT_all - kb, a.bps * 4));     // pipeline steps (one group each)
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) {
@@ -230,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int pbox = 0;
       for (; pbox < kPStages && pbox < nbox; ++pbox) {
         mbar_arrive_expect_tx(&p_full[pbox], kPBytes);
-        tma_load_2d(sP + pbox * kPBytes, &wmap, pbox * 128, (int)n0, &p_full[pbox]);
+        tma_load_2d(sP + pbox * kPBytes, &wmap, (box0 + pbox) * 128, (int)n0, &p_full[pbox]);
       }
       pdl_wait();
       for (int k = 0; k < KT; ++k) {
@@ -238,14 +253,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (uint32_t)(k / kStages) & 1u;
         mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
         mbar_arrive_expect_tx(&b_full[s], kBBytes);
-        tma_load_2d(sB + s * kBBytes, &xmap, k * kGroup, m0, &b_full[s]);
-        if constexpr (kXTiles == 2) tma_load_2d(sB + s * kBBytes + BN * 128, &xmap_lo, k * kGroup, m0, &b_full[s]);
+        tma_load_2d(sB + s * kBBytes, &xmap, (kb + k) * kGroup, m0, &b_full[s]);
+        if constexpr (kXTiles == 2)
+          tma_load_2d(sB + s * kBBytes + BN * 128, &xmap_lo, (kb + k) * kGroup, m0, &b_full[s]);
         if ((k & 3) == 3 && pbox < nbox) {  // refill the packed ring
           const int p = pbox % kPStages;
           const uint32_t pph = (uint32_t)(pbox / kPStages) & 1u;
           mbar_wait(&p_empty[p], pph ^ 1u, &g_gemm_tc_error);
           mbar_arrive_expect_tx(&p_full[p], kPBytes);
-          tma_load_2d(sP + p * kPBytes, &wmap, pbox * 128, (int)n0, &p_full[p]);
+          tma_load_2d(sP + p * kPBytes, &wmap, (box0 + pbox) * 128, (int)n0, &p_full[p]);
           ++pbox;
         }
       }
@@ -284,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t row = n0 + r;
     const bool row_ok = row < a.N;
     const int64_t G = a.K / kGroup;
-    const __half* srow = a.scales + (row_ok ? row : 0) * G;
-    const int64_t zrow = (row_ok ? row : 0) * G;
+    const __half* srow = a.scales + (row_ok ? row : 0) * G + kb;
+    const int64_t zrow = (row_ok ? row : 0) * G + kb;
     const uint32_t sP_addr = smem_addr(sP);
     const uint32_t t_lane = (uint32_t)(quarter * 32) << 16;
     const int nbox = (KT + 3) / 4;
@@ -352,7 +368,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int c0 = sub * kCols; c0 < (sub + 1) * kCols && c0 < BN; c0 += 32) {
       uint32_t v[32];
       tmem_ld32(tmem_d + t_lane + (uint32_t)c0, v);
-      if (a.tma_out) {
+      if (a.ksplit > 1) {  // partial sums stay in shared memory for the cluster reduction
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[(c0 + j) * kTileN + er] = KT > 0 ? __uint_as_float(v[j]) : 0.f;
+      } else if (a.tma_out) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float f = __uint_as_float(v[j]) + bv;
@@ -380,6 +399,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (a.ksplit > 1) {
+    // K split: the cluster's CTAs sum their partial tiles over distributed
+    // shared memory; CTA z finishes rows [z * 128 / ksplit, ...) of the tile.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every partial tile is written
+    if (warp >= 2) {
+      const int nranks = (int)cluster.num_blocks();
+      const int per = (kTileN + nranks - 1) / nranks;
+      const int rlo = (int)cluster.block_rank() * per;
+      const int rows = min(kTileN, rlo + per) - rlo;
+      for (int i = (int)threadIdx.x - 64; rows > 0 && i < rows * BN; i += 32 * kDeqWarps) {
+        const int c = i / rows, r = rlo + (i - c * rows);
+        float sum = 0.f;
+        for (int q = 0; q < nranks; ++q) sum += cluster.map_shared_rank(part, q)[c * kTileN + r];
+        const int m = m0 + c;
+        const int64_t n = n0 + r;
+        if (m < a.M && n < a.N) {
+          const float b = a.bias ? load_as_f32(a.bias, a.bias_dtype, n) : 0.f;
+          store_from_f32(a.out, a.out_dtype, (int64_t)m * a.N + n, sum + b);
+        }
+      }
+    }
+    cluster.sync();  // no CTA leaves while a peer still reads its partials
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -389,35 +434,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-size_t smem_bytes(int BN, int x_tiles) {
+size_t smem_bytes(int BN, int x_tiles, int ksplit) {
   return 1024 + (size_t)kStages * x_tiles * BN * 128 + (size_t)kPStages * kPBytes +
-         (3 * kStages + 2 * kPStages + 1) * sizeof(uint64_t) + 16;
+         (3 * kStages + 2 * kPStages + 1) * sizeof(uint64_t) + 16 +
+         (ksplit > 1 ? (size_t)BN * kTileN * sizeof(float) : 0);
 }
 
 template <int XT, int BN>
 cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                       const CUtensorMap& omap, const Args& a, cudaStream_t stream, bool pdl) {
-  const size_t smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1);
+  const size_t smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1, a.ksplit);
   auto kernel = gemm_tc_kernel<XT, BN>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Room for the K split's partial tile where one is planned (tiles <= 128 wide).
+    const size_t max_smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1, BN <= 128 ? 2 : 1);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)max_smem);
     if (e != cudaSuccess) return e;
     configured |= bit;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), 1);
+  cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), (unsigned)a.ksplit);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (a.ksplit > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = (unsigned)a.ksplit;
+    ++n;
+  }
   cfg.attrs = attrs;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, xmap_lo, omap, a);
 }
 
@@ -431,6 +490,23 @@ cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUt
       if constexpr (XT == QI4_DTYPE_F32) return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
       else return launch_bn<XT, 256>(wmap, xmap, xmap_lo, omap, a, s, pdl);
   }
+}
+
+// K split for M <= 128 when the grid is smaller than the SM count (few
+// weight tiles x one token tile, each otherwise running every stage of K in
+// series): up to 8 CTAs per cluster, each at least one packed box (4
+// groups), partial tiles reduced over distributed shared memory. Measured on
+// B200: 1.7x at M = 32, 1.2x at M = 128; at larger M the per-CTA work already
+// hides the pipeline latency and the cluster reduction only costs (k/v at
+// M = 2048 went from 14 to 23 us), so K stays whole there.
+void plan_ksplit(Args& a, int num_sms) {
+  const int nbox = (int)((a.K / kGroup + 3) / 4);
+  const int64_t tiles = ((a.N + kTileN - 1) / kTileN) * ((a.M + a.BN - 1) / a.BN);
+  int ks = 1;
+  if (a.M <= 128 && a.BN <= 128 && tiles < num_sms && nbox >= 2)
+    ks = (int)std::min<int64_t>({8, (int64_t)nbox, (num_sms + tiles - 1) / tiles});
+  a.bps = (nbox + ks - 1) / ks;
+  a.ksplit = (nbox + a.bps - 1) / a.bps;  // every CTA of the cluster gets at least one box
 }
 
 // FP32 activations -> two bf16 arrays with x = hi + lo (hi = bf16(x),
@@ -491,6 +567,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
       }
     }
   }
+  plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&xmap_lo, 0, sizeof(xmap_lo));
   memset(&omap, 0, sizeof(omap));
@@ -524,7 +601,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
     // Output tile by TMA store when the row pitch allows a tensor map (a
     // multiple of 16 bytes, 16-byte-aligned base); otherwise direct stores.
     const int osz = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
-    a.tma_out = ((N * osz) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+    a.tma_out = a.ksplit == 1 && ((N * osz) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
                 tensor_map_2d(&omap, out,
                               x_dtype == QI4_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                               : x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -599,6 +676,7 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
   a.out = out;
   a.out_dtype = QI4_DTYPE_F32;
   a.BN = M > 64 ? 128 : 64;
+  plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&omap, 0, sizeof(omap));
   // Every element of the hi / lo arrays that the GEMM reads is written by the
@@ -617,7 +695,7 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
       !tensor_map_2d(&xmap_lo, lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
                      kGroup, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  a.tma_out = ((N * 4) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+  a.tma_out = a.ksplit == 1 && ((N * 4) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
               tensor_map_2d(&omap, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)N, (uint64_t)M,
                             (uint64_t)N * 4, kTileN, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_NONE);
   return launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, false);

@@ -64,6 +64,31 @@ def quantize_symmetric_rtn_torch(weight: torch.Tensor, group_size: int = 64):
     return packed.reshape(-1, 1).contiguous(), scale.to(torch.float16).contiguous()
 
 
+def quantize_asymmetric_rtn_torch(weight: torch.Tensor, group_size: int = 64):
+    """W4 asymmetric RTN on any device, as the reference's
+    ``quantize_asymmetric_rtn`` (src/qwen_int4/quantization.py:114-162): per
+    group, scale = max(hi - lo, 1e-5) / 15 with lo <= 0 <= hi, zero =
+    clip(round(-lo / scale), 0, 15), code = clip(round(w / scale) + zero, 0,
+    15); codes and zeros are stored shifted by -8 as signed INT4 (an odd zero
+    count is padded with one zero nibble). Returns (packed uint8 [N*K/2, 1],
+    fp16 scales [N, K/group], packed zeros uint8 [(N*G+1)//2, 1])."""
+    n, k = weight.shape
+    g = weight.to(torch.float32).reshape(n, k // group_size, group_size)
+    lo = torch.clamp(g.amin(dim=-1), max=0.0)
+    hi = torch.clamp(g.amax(dim=-1), min=0.0)
+    scale = torch.clamp(hi - lo, min=1e-5) / 15.0
+    uzero = torch.clamp(torch.round(-lo / scale), 0, 15)
+    ucode = torch.clamp(torch.round(g / scale.unsqueeze(-1)) + uzero.unsqueeze(-1), 0, 15)
+    codes = (ucode.to(torch.int16) - 8).reshape(n, k)
+    zeros = (uzero.to(torch.int16) - 8).reshape(-1)
+    if zeros.numel() % 2:
+        zeros = torch.cat([zeros, zeros.new_zeros(1)])
+    pack = lambda v: ((v[0::2] & 0xF) | ((v[1::2] & 0xF) << 4)).to(torch.uint8)
+    packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8)
+    return (packed.reshape(-1, 1).contiguous(), scale.to(torch.float16).contiguous(),
+            pack(zeros).reshape(-1, 1).contiguous())
+
+
 @torch.no_grad()
 def build_random_qwen2(config=None, *, device="cuda", seed: int = 0, backend: str = "b200"):
     """Reference ``QwenInt4ForCausalLM`` with random W4G64 RTN weights on ``device``.

@@ -176,3 +176,20 @@ def test_gather_with_a_lost_rank_fails_instead_of_hanging(tmp_path):
     except Exception:
         pass  # a rank may also exit with an error; what matters is rank 0's outcome
     assert result.read_text() == "error"
+
+
+def test_torch_asymmetric_quantizer_matches_the_oracle_bytes():
+    """The device-agnostic torch quantiser used to build synthetic asymmetric
+    weights gives the oracle's (reference-pinned) bytes on CPU."""
+    import importlib
+
+    q2 = importlib.import_module("qwen2-int4-systems_b200.qwen2")
+    rng = np.random.default_rng(11)
+    for n, k in ((8, 128), (3, 192), (16, 64)):
+        w = rng.standard_normal((n, k), dtype=np.float32) * 0.05
+        w[0, :64] = 0.0  # an all-zero group
+        qw, sc, z = q2.quantize_asymmetric_rtn_torch(torch.from_numpy(w))
+        oq, osc, oz = orc.quantize_asymmetric_rtn(w)
+        np.testing.assert_array_equal(qw.numpy(), oq)
+        np.testing.assert_array_equal(sc.numpy(), osc)
+        np.testing.assert_array_equal(z.numpy(), oz)
