@@ -142,6 +142,20 @@ QI4_API int qi4_w4g64_linear_multi(const void* x, int x_dtype, int64_t M, int64_
                                    const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
                                    void* const* outs, const int64_t* Ns, void* stream);
 
+/* Fused gate/up projection + SwiGLU of a decoder MLP: out[M, N] (FP32) =
+ * silu(g) * u with g = x @ W_gate^T and u = x @ W_up^T, each rounded to the
+ * activation dtype first (the dtype QuantLinear returns) - the tensor the
+ * reference MLP hands to down_proj (src/qwen_int4/model.py:133-135, which
+ * computes F.silu(gate(x).float()) * up(x).float()). Both matrices are
+ * canonical W4G64 with the same K and N; no bias. For M <= 16 one GEMV launch
+ * owns the same output rows of both matrices; larger M runs both projections
+ * on the tensor cores, then an elementwise kernel. No reference counterpart as
+ * a single call. */
+QI4_API int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight_gate,
+                                   const uint16_t* scales_gate_f16, const uint8_t* zeros_gate,
+                                   const uint8_t* qweight_up, const uint16_t* scales_up_f16,
+                                   const uint8_t* zeros_up, float* out, int64_t N, void* stream);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
  * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8 or 16,

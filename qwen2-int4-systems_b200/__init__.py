@@ -10,6 +10,7 @@ from ._lib import ALGO_AUTO, ALGO_GEMV, ALGO_GEMV_FMA, ALGO_TC
 from .backends import (
     SUPPORTED_BACKENDS,
     b200_w4g64_linear,
+    b200_w4g64_gate_up_silu,
     b200_w4g64_linear_multi,
     dequantize_canonical_w4g64_b200,
     linear_canonical_w4g64_b200,
@@ -21,6 +22,7 @@ from .linear import QuantLinear
 
 __all__ = [
     "ALGO_AUTO", "ALGO_GEMV", "ALGO_GEMV_FMA", "ALGO_TC", "QuantLinear", "SUPPORTED_BACKENDS",
-    "b200_w4g64_linear", "b200_w4g64_linear_multi", "dequantize_canonical_w4g64_b200", "linear_canonical_w4g64_b200",
+    "b200_w4g64_gate_up_silu", "b200_w4g64_linear", "b200_w4g64_linear_multi",
+    "dequantize_canonical_w4g64_b200", "linear_canonical_w4g64_b200",
     "register_with_reference", "set_value_checks", "unpack_canonical_signed_int4_b200",
 ]

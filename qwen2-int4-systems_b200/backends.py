@@ -212,6 +212,40 @@ def b200_w4g64_linear_multi(x: torch.Tensor, layers) -> list[torch.Tensor]:
     return [o.reshape(*x.shape[:-1], l.out_features) for o, l in zip(outs, layers)]
 
 
+def b200_w4g64_gate_up_silu(x: torch.Tensor, gate_proj, up_proj) -> torch.Tensor:
+    """``F.silu(gate_proj(x).float()) * up_proj(x).float()`` in one call: the
+    FP32 tensor the reference MLP passes to ``down_proj``
+    (src/qwen_int4/model.py:133-135). ``gate_proj`` / ``up_proj`` carry the
+    QuantLinear buffers and sizes (same in/out features, no bias). Each
+    projection is rounded to ``x.dtype`` before the SwiGLU, as QuantLinear
+    returns it. No reference counterpart as a single call.
+    """
+    k, n = gate_proj.in_features, gate_proj.out_features
+    if up_proj.in_features != k or up_proj.out_features != n:
+        raise ValueError("gate_proj and up_proj must have the same shape")
+    if getattr(gate_proj, "bias", None) is not None or getattr(up_proj, "bias", None) is not None:
+        raise ValueError("the fused gate/up call takes projections without bias")
+    for l in (gate_proj, up_proj):
+        _validate_linear(x, l.qweight, l.scales, l.zeros, None, n, k, GROUP_SIZE, "canonical")
+    lib = _require_cuda()
+    x2 = _aligned(x.reshape(-1, k))
+    out = torch.empty((x2.shape[0], n), dtype=torch.float32, device=x.device)
+    if x2.shape[0]:
+        device = x2.device
+        if torch.cuda.current_device() != device.index:
+            with torch.cuda.device(device):
+                return b200_w4g64_gate_up_silu(x, gate_proj, up_proj)
+        if gate_proj.qweight.data_ptr() % 16 or up_proj.qweight.data_ptr() % 16:
+            raise ValueError("qweight storage must be 16-byte aligned for the B200 kernels")
+        rc = lib.qi4_w4g64_gate_up_silu(
+            x2.data_ptr(), _DTYPE_CODE[x2.dtype], x2.shape[0], k,
+            gate_proj.qweight.data_ptr(), gate_proj.scales.data_ptr(), gate_proj.zeros.data_ptr(),
+            up_proj.qweight.data_ptr(), up_proj.scales.data_ptr(), up_proj.zeros.data_ptr(),
+            out.data_ptr(), n, _stream(device))
+        _lib.check(rc, "qi4_w4g64_gate_up_silu")
+    return out.reshape(*x.shape[:-1], n)
+
+
 def linear_canonical_w4g64_b200(
     activations: torch.Tensor,
     qweight: torch.Tensor,

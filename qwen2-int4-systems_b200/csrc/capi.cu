@@ -245,11 +245,68 @@ static int linear_multi_impl(const void* x, int x_dtype, int64_t M, int64_t K, i
                       "w4g64 grouped GEMV");
 }
 
+static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qw_gate,
+                             const uint16_t* sc_gate, const uint8_t* z_gate, const uint8_t* qw_up,
+                             const uint16_t* sc_up, const uint8_t* z_up, float* out, int64_t N, void* stream_ptr) {
+  clear_error();
+  int rc = validate_linear(x, x_dtype, M, K, qw_gate, sc_gate, nullptr, QI4_DTYPE_NONE, out, N);
+  if (!rc) rc = validate_linear(x, x_dtype, M, K, qw_up, sc_up, nullptr, QI4_DTYPE_NONE, out, N);
+  if (rc) return rc;
+  if (!aligned(out, 4)) {
+    set_error("out (FP32) must be 4-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  DeviceInfo info;
+  rc = current_device(info);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const uint8_t* qws[2] = {qw_gate, qw_up};
+  const uint16_t* scs[2] = {sc_gate, sc_up};
+  const uint8_t* zs[2] = {z_gate, z_up};
+  if (M <= kGemvMaxM) {
+    const MmaGemvPlan plan = plan_gemv_swiglu(M, K, x_dtype);
+    if (plan.rows == 0) {
+      set_error("no fused gate/up launch shape fits K=%lld", (long long)K);
+      return QI4_ERR_SHAPE;
+    }
+    return check_launch(launch_gemv_swiglu(x, x_dtype, M, K, qws, scs, zs, out, N, stream, true, plan),
+                        "w4g64 fused gate/up SwiGLU GEMV");
+  }
+  // Prefill sizes: both projections on the tensor cores into scratch (their
+  // outputs in the activation dtype, as QuantLinear returns them), then the
+  // elementwise SwiGLU.
+  const size_t xsize = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
+  const size_t bytes = (size_t)M * (size_t)N * xsize;
+  const size_t half = (bytes + 255) / 256 * 256;
+  void* scratch = nullptr;
+  if (cudaMallocAsync(&scratch, 2 * half, stream) != cudaSuccess) {
+    set_error("scratch allocation of %zu bytes failed", 2 * half);
+    return QI4_ERR_DEVICE;
+  }
+  void* g = scratch;
+  void* u = static_cast<char*>(scratch) + half;
+  rc = linear_impl(x, x_dtype, M, K, qw_gate, sc_gate, z_gate, nullptr, QI4_DTYPE_NONE, g, N, stream_ptr,
+                   QI4_ALGO_AUTO, 1);
+  if (!rc)
+    rc = linear_impl(x, x_dtype, M, K, qw_up, sc_up, z_up, nullptr, QI4_DTYPE_NONE, u, N, stream_ptr, QI4_ALGO_AUTO, 1);
+  if (!rc) rc = check_launch(launch_swiglu_elementwise(g, u, x_dtype, out, M * N, stream, info.sms), "SwiGLU");
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+
 }  // namespace qi4
 
 using namespace qi4;
 
 extern "C" {
+
+int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight_gate,
+                           const uint16_t* scales_gate_f16, const uint8_t* zeros_gate, const uint8_t* qweight_up,
+                           const uint16_t* scales_up_f16, const uint8_t* zeros_up, float* out, int64_t N,
+                           void* stream) {
+  return gate_up_silu_impl(x, x_dtype, M, K, qweight_gate, scales_gate_f16, zeros_gate, qweight_up, scales_up_f16,
+                           zeros_up, out, N, stream);
+}
 
 int qi4_w4g64_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
                            const uint8_t* const* qweights, const uint16_t* const* scales_f16,

@@ -289,14 +289,16 @@ __host__ __device__ constexpr int x_stride_bytes(int bps, bool f32) { return bps
 // and zero points of four consecutive groups of a row are one 8-byte and one
 // 2-byte load when the row length in groups is a multiple of four.
 template <int XT>
-__device__ __forceinline__ void build_table(const Args& a, const Mat& mt, TableEntry* table, int tstride, int64_t row0, int g0,
-                                            int gs, int tid, int nthreads) {
+__device__ __forceinline__ void build_table(const Args& a, const Mat& mt0, const Mat* mt1, TableEntry* table,
+                                            int tstride, int64_t row0, int g0, int gs, int tid, int nthreads) {
   const int R = a.rows;
   const int nch = (gs + 3) >> 2;
   const bool vec = (a.G & 3) == 0;
   for (int e = tid; e < R * nch; e += nthreads) {
     const int r = e & (R - 1), g = (e >> a.rows_log2) << 2;
-    const int64_t row = row0 + r;
+    // mt1 (gate/up SwiGLU): rows 16..31 of the tile are the second matrix's rows row0..row0+15.
+    const Mat& mt = (mt1 && r >= 16) ? *mt1 : mt0;
+    const int64_t row = row0 + (mt1 ? (r & 15) : r);
     float s[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t znib = 0;  // the four groups' stored zero nibbles (two's complement; 0 when absent)
     if (row < mt.N) {
@@ -323,6 +325,17 @@ __device__ __forceinline__ void build_table(const Args& a, const Mat& mt, TableE
       if (g + j < gs)
         t[j] = TableEntry{s[j], Fmt<XT>::kMagic + (((znib >> (4 * j)) & 0xF) ^ 0x8u) * 0x00010001u};
   }
+}
+
+// v rounded to the activation dtype (identity for FP32).
+template <int XT>
+__device__ __forceinline__ float round_act(float v) {
+  if constexpr (XT == QI4_DTYPE_BF16)
+    return __bfloat162float(__float2bfloat16_rn(v));
+  else if constexpr (XT == QI4_DTYPE_F16)
+    return __half2float(__float2half_rn(v));
+  else
+    return v;
 }
 
 // The output has the activations' dtype (FP32 for FP32 activations).
@@ -380,11 +393,14 @@ __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* a
   }
 }
 
-template <int XT, int NT, int WARPS, int PRE>
+template <int XT, int NT, int WARPS, int PRE, bool SW = false>
 __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const Args a) {
   // PRE > 0: every warp has at most PRE groups, expanded into registers
   // before the dependency wait (single-wave grids, whose CTAs start early).
+  // SW: fused gate/up + SwiGLU. A CTA owns the same 16 output rows of both
+  // matrices (its 32-row tile: 16 gate rows, then 16 up rows) and writes
+  // silu(g) * u in FP32.
   constexpr int kThr = WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
@@ -402,7 +418,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   const int m = (a.nmats > 1 && tile >= a.tiles_end[0]) + (a.nmats > 2 && tile >= a.tiles_end[1]);
   const Mat& mt = m == 0 ? a.mat[0] : (m == 1 ? a.mat[1] : a.mat[2]);
   const CUtensorMap* wmap = m == 0 ? &wmap0 : (m == 1 ? &wmap1 : &wmap2);
-  const int64_t row0 = (int64_t)(tile - (m == 0 ? 0 : a.tiles_end[m - 1])) * R;
+  const int64_t row0 = SW ? (int64_t)tile * 16 : (int64_t)(tile - (m == 0 ? 0 : a.tiles_end[m - 1])) * R;
 
   const int tstride = a.boxes_per_split * kGroupsPerBox + 1;  // odd stride: conflict-free table reads
   const int copies = (nbox + (1 << a.copy_log2) - 1) >> a.copy_log2;
@@ -417,7 +433,17 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   // griddepcontrol.wait, overlapping the previous kernels of a chain.
   pdl_launch_dependents();
   const int tid = threadIdx.x;
-  if (tid == 0 && nbox > 0) {
+  if (SW && tid == 0 && nbox > 0) {
+    // One barrier per box, completed by a 16-row copy from each matrix.
+    for (int b = 0; b < nbox; ++b) mbar_init(bars + b, 1);
+    fence_barrier_init();
+    for (int b = 0; b < nbox; ++b) {
+      mbar_arrive_expect_tx(bars + b, (uint32_t)(R * kBoxBytes));
+      tma_load_2d(wsm + (size_t)b * R * kBoxBytes, &wmap0, (box0 + b) * kBoxBytes, (int)row0, bars + b);
+      tma_load_2d(wsm + (size_t)b * R * kBoxBytes + 16 * kBoxBytes, &wmap1, (box0 + b) * kBoxBytes, (int)row0,
+                  bars + b);
+    }
+  } else if (tid == 0 && nbox > 0) {
     // One 3-D copy brings (1 << copy_log2) boxes of the R rows, box-major;
     // boxes past the end of a row arrive zero-filled (and are never read).
     for (int c = 0; c < copies; ++c) mbar_init(bars + c, 1);
@@ -431,7 +457,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
         tma_load_2d(wsm + (size_t)c * R * kBoxBytes, wmap, (box0 + c) * kBoxBytes, (int)row0, bars + c);
     }
   }
-  build_table<XT>(a, mt, table, tstride, row0, g0, gs, tid, kThr);
+  build_table<XT>(a, mt, SW ? &a.mat[1] : nullptr, table, tstride, row0, g0, gs, tid, kThr);
   __syncthreads();  // barriers initialised, table complete
 
   const int warp = tid >> 5, lane = tid & 31;
@@ -544,6 +570,28 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
     for (int q = 0; q < 4; ++q)
       part[((size_t)kp * R + r_lo + (q < 2 ? 0 : 8)) * ld + n * 8 + 2 * tq + (q & 1)] = acc[n][q];
   __syncthreads();
+  if constexpr (SW) {
+    // g and u are rounded to the activation dtype (the projections' output
+    // dtype), then silu(g) * u in FP32, as the reference MLP computes it.
+    float* out = static_cast<float*>(mt.out);
+    for (int i = tid; i < 16 * a.M; i += kThr) {
+      const int tok = i >> 4, r = i & 15;
+      const int64_t row = row0 + r;
+      float g = 0.f, u = 0.f;
+#pragma unroll
+      for (int q = 0; q < WARPS; ++q)
+        if (q < KP) {
+          g += part[((size_t)q * R + r) * ld + tok];
+          u += part[((size_t)q * R + 16 + r) * ld + tok];
+        }
+      if (row < mt.N) {
+        g = round_act<XT>(g);
+        u = round_act<XT>(u);
+        out[(int64_t)tok * mt.N + row] = g / (1.0f + expf(-g)) * u;
+      }
+    }
+    return;
+  }
   const bool split = gridDim.y > 1;
   for (int i = tid; i < R * a.M; i += kThr) {
     const int tok = i >> a.rows_log2, r = i - (tok << a.rows_log2);
@@ -595,9 +643,9 @@ size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32, int copy_l
   return 1024 + (size_t)alloc_boxes(bps, copy_log2) * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
 }
 
-template <int XT, int NT, int WARPS, int PRE>
+template <int XT, int NT, int WARPS, int PRE, bool SW = false>
 cudaError_t launch_t(const CUtensorMap* maps, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
-  auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE>;
+  auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE, SW>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -779,6 +827,100 @@ cudaError_t launch_gemv_mma(const void* x, int x_dtype, int64_t M, int64_t K, co
                             void* out, int64_t N, cudaStream_t stream, bool pdl, const MmaGemvPlan& p) {
   return launch_gemv_mma_multi(x, x_dtype, M, K, 1, &qweight, &scales, &zeros, &bias, bias_dtype, &out, &N, stream,
                                pdl, p);
+}
+
+namespace {
+
+template <int XT>
+cudaError_t launch_swiglu_x(const CUtensorMap* maps, const Args& a, int nt, cudaStream_t s, bool pdl) {
+  return nt <= 1 ? launch_t<XT, 1, 8, 0, true>(maps, a, 1, s, pdl) : launch_t<XT, 2, 8, 0, true>(maps, a, 1, s, pdl);
+}
+
+// out = silu(g) * u in FP32 from the two projections' outputs (activation
+// dtype), for the tensor-core route of the fused call.
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u,
+                                                     float* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float gv = static_cast<float>(g[i]), uv = static_cast<float>(u[i]);
+    out[i] = gv / (1.0f + expf(-gv)) * uv;
+  }
+}
+
+}  // namespace
+
+MmaGemvPlan plan_gemv_swiglu(int64_t M, int64_t K, int x_dtype) {
+  const int G = (int)(K / kGroup);
+  MmaGemvPlan p{};
+  p.rows = 32;  // 16 gate rows + 16 up rows
+  p.warps = 8;
+  p.ksplit = 1;
+  p.boxes_per_split = (G + kGroupsPerBox - 1) / kGroupsPerBox;
+  p.nt = M <= 8 ? 1 : 2;
+  p.pre = 0;
+  p.three_d = 0;
+  p.copy_log2 = 0;
+  p.smem = smem_bytes(p.rows, p.warps, p.boxes_per_split, p.nt, (int)M, x_dtype == QI4_DTYPE_F32, 0);
+  if (p.smem > 200 * 1024) p.rows = 0;
+  return p;
+}
+
+cudaError_t launch_gemv_swiglu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* const* qweights,
+                               const uint16_t* const* scales, const uint8_t* const* zeros, float* out, int64_t N,
+                               cudaStream_t stream, bool pdl, const MmaGemvPlan& p) {
+  CUtensorMap maps[kMaxMats];
+  for (int i = 0; i < 2; ++i)
+    if (!tensor_map_2d(&maps[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
+                       (uint64_t)(K / 2), kBoxBytes, 16, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  maps[2] = maps[1];
+  Args a{};
+  a.x = x;
+  a.M = (int)M;
+  a.K = K;
+  a.nmats = 2;
+  a.bias_dtype = QI4_DTYPE_NONE;
+  a.rows = p.rows;
+  a.rows_log2 = __builtin_ctz((unsigned)p.rows);
+  a.boxes_per_split = p.boxes_per_split;
+  a.copy_log2 = 0;
+  a.three_d = 0;
+  a.G = (int)(K / kGroup);
+  const int tiles = (int)((N + 15) / 16);
+  for (int i = 0; i < kMaxMats; ++i) {
+    const int j = i < 2 ? i : 1;
+    a.mat[i].scales = reinterpret_cast<const __half*>(scales[j]);
+    a.mat[i].zeros = zeros[j];
+    a.mat[i].bias = nullptr;
+    a.mat[i].out = out;
+    a.mat[i].N = N;
+    a.tiles_end[i] = tiles;
+  }
+  switch (x_dtype) {
+    case QI4_DTYPE_F16: return launch_swiglu_x<QI4_DTYPE_F16>(maps, a, p.nt, stream, pdl);
+    case QI4_DTYPE_BF16: return launch_swiglu_x<QI4_DTYPE_BF16>(maps, a, p.nt, stream, pdl);
+    default: return launch_swiglu_x<QI4_DTYPE_F32>(maps, a, p.nt, stream, pdl);
+  }
+}
+
+cudaError_t launch_swiglu_elementwise(const void* g, const void* u, int dtype, float* out, int64_t n,
+                                      cudaStream_t stream, int num_sms) {
+  if (n <= 0) return cudaSuccess;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms * 8);
+  switch (dtype) {
+    case QI4_DTYPE_F16:
+      swiglu_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(g), static_cast<const __half*>(u),
+                                                         out, n);
+      break;
+    case QI4_DTYPE_BF16:
+      swiglu_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(g),
+                                                                static_cast<const __nv_bfloat16*>(u), out, n);
+      break;
+    default:
+      swiglu_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float*>(g), static_cast<const float*>(u),
+                                                        out, n);
+  }
+  return cudaGetLastError();
 }
 
 int read_gemv_mma_error(cudaStream_t stream) {

@@ -33,6 +33,16 @@ cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t
                                   const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
                                   void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl,
                                   const MmaGemvPlan& plan);
+// Fused gate/up + SwiGLU for M <= 16: out[M, N] (FP32) = silu(g) * u with g, u
+// the two projections of x rounded to the activation dtype (the reference
+// MLP's composition). qweights/scales/zeros hold {gate, up}.
+MmaGemvPlan plan_gemv_swiglu(int64_t M, int64_t K, int x_dtype);
+cudaError_t launch_gemv_swiglu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* const* qweights,
+                               const uint16_t* const* scales, const uint8_t* const* zeros, float* out, int64_t N,
+                               cudaStream_t stream, bool pdl, const MmaGemvPlan& plan);
+// out[i] = silu(g[i]) * u[i] in FP32 from two activation-dtype arrays.
+cudaError_t launch_swiglu_elementwise(const void* g, const void* u, int dtype, float* out, int64_t n,
+                                      cudaStream_t stream, int num_sms);
 // Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
 int read_gemv_mma_error(cudaStream_t stream);
 

@@ -180,3 +180,19 @@ def test_grouped_linear_rejects_bad_groups_without_a_gpu(b200):
         b200.b200_w4g64_linear_multi(x, [lay, other])
     with pytest.raises(ValueError, match="CUDA tensors"):
         b200.b200_w4g64_linear_multi(x, [lay, lay])
+
+
+def test_fused_gate_up_rejects_mismatched_projections_without_a_gpu(b200):
+    from types import SimpleNamespace
+
+    qw, sc, z = _tensors(64, 128)
+    gate = SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=128, out_features=64)
+    other = SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=192, out_features=64)
+    biased = SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=torch.zeros(64), in_features=128, out_features=64)
+    x = torch.ones(1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="same shape"):
+        b200.b200_w4g64_gate_up_silu(x, gate, other)
+    with pytest.raises(ValueError, match="without bias"):
+        b200.b200_w4g64_gate_up_silu(x, gate, biased)
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        b200.b200_w4g64_gate_up_silu(x, gate, gate)

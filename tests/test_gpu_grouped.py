@@ -90,3 +90,55 @@ def test_grouped_equals_single_calls_for_the_same_plan(b200, cuda_device):
     for g, s in zip(grouped, single):
         assert torch.equal(g, s)
     assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def _swiglu_ref(x, gate, up):
+    """silu(round(gate(x))) * round(up(x)) in float64 from the oracle, the
+    rounding to x's dtype standing in for QuantLinear's output dtype."""
+    xs = x.float().cpu().numpy().reshape(-1, gate.in_features)
+    outs = []
+    for l in (gate, up):
+        qw, sc, z, _ = l.np
+        y = orc.linear(xs, qw, sc, z, None, out_features=l.out_features, in_features=l.in_features,
+                       accumulate="f64")
+        outs.append(torch.from_numpy(y).to(x.dtype).double().numpy())
+    g, u = outs
+    return g / (1.0 + np.exp(-g)) * u, g, u
+
+
+def _swiglu_budget(ref, g, u, dtype, tensor_cores):
+    # One rounding of g or u to x's dtype may land on the neighbouring value
+    # (the kernel's and the float64 oracle's sums differ far below that step):
+    # d(silu(g) u) <= 1.1 |u| dg + |g| du, dg and du one step each.
+    step = {torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10, torch.float32: 1e-5}[dtype]
+    budget = 1e-3 + step * (np.abs(ref) + 2.1 * np.abs(g * u))
+    if tensor_cores:
+        # g and u carry the GEMM tolerance (2e-2 absolute: the weight rounded once).
+        budget = budget + 2e-2 * (1.1 * np.abs(u) + np.abs(g) + 2e-2)
+    return budget
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m", [1, 5, 16, 40])
+def test_fused_gate_up_silu_matches_the_reference_composition(b200, cuda_device, dtype, m):
+    from importlib import import_module
+
+    gate, up = (_layer(8960 if m < 40 else 1000, 1536, 60 + i, cuda_device, i == 1) for i in range(2))
+    x = torch.randn(m, 1536, generator=torch.Generator().manual_seed(m)).to(dtype).to(cuda_device)
+    got = b200.b200_w4g64_gate_up_silu(x, gate, up)
+    assert got.dtype == torch.float32 and got.shape == (m, gate.out_features)
+    ref, g, u = _swiglu_ref(x, gate, up)
+    err = np.abs(got.cpu().numpy().astype(np.float64) - ref)
+    assert np.all(err <= _swiglu_budget(ref, g, u, dtype, m > 16)), f"max err {err.max():.3e}"
+    lib = import_module(b200.__name__ + "._lib").load()
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_fused_gate_up_silu_ragged_rows_and_k(b200, cuda_device):
+    gate, up = (_layer(100, 192, 70 + i, cuda_device, True) for i in range(2))
+    x = torch.randn(2, 3, 192, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(cuda_device)
+    got = b200.b200_w4g64_gate_up_silu(x, gate, up)
+    ref, g, u = _swiglu_ref(x, gate, up)
+    assert got.shape == (2, 3, 100)
+    err = np.abs(got.reshape(-1, 100).cpu().numpy().astype(np.float64) - ref)
+    assert np.all(err <= _swiglu_budget(ref, g, u, torch.bfloat16, False)), f"max err {err.max():.3e}"
