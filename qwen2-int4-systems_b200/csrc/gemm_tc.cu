@@ -47,16 +47,22 @@ __device__ int g_gemm_tc_error;
 
 namespace {
 
-constexpr int kStages = 3;      // A (dequantised) + B (activations) stages
+// A (dequantised, in TMEM) + B (activations, in shared memory) stages in
+// flight. Measured on B200 at M = 2048 over the seven Qwen2 shapes: 3 stages
+// 700 TFLOP/s aggregate, 4 stages 734, 5 stages 717.
+constexpr int kStages = 4;
 constexpr int kPStages = 2;     // packed-weight boxes (4 groups each)
 constexpr int kTileN = 128;     // weight rows per tile (UMMA M)
-constexpr int kDeqWarps = 16;
-constexpr int kThreads = 64 + 32 * kDeqWarps;  // producer + MMA + dequant/epilogue warps
+// Dequantise/epilogue warps per CTA: 16 (one CTA per SM, tiles up to 256
+// tokens) or 8 (128-token tiles, two CTAs per SM, so that one CTA's prologue
+// and epilogue overlap the other's main loop). Threads: producer + MMA warps
+// plus these.
+__host__ __device__ constexpr int gemm_threads(int dw) { return 64 + 32 * dw; }
 
 // Tensor-memory columns: the FP32 accumulator (BN) plus kStages A stages of 32
 // columns (64 bf16 K elements of 128 rows), rounded up to a power of two.
 __host__ __device__ constexpr uint32_t tmem_cols(int bn) {
-  return bn + 32 * 3 <= 128 ? 128u : (bn + 32 * 3 <= 256 ? 256u : 512u);
+  return bn + 32 * kStages <= 128 ? 128u : (bn + 32 * kStages <= 256 ? 256u : 512u);
 }
 constexpr int kABytes = kTileN * 128;   // one group of 128 rows in bf16: 16 KB
 constexpr int kPBytes = kTileN * 128;   // one packed box: 128 rows x 128 B
@@ -72,6 +78,7 @@ struct Args {
   int out_dtype;
   int BN;
   int tma_out;  // 1: output tile staged in shared memory and written by one TMA store
+  int dw;       // dequantise/epilogue warps per CTA: 16 or 8 (two CTAs per SM, BN <= 128)
   int ksplit;   // CTAs per cluster along K (grid z); > 1 reduces FP32 partial tiles over DSMEM
   int bps;      // packed 128-byte boxes (4 groups) per K split
 };
@@ -108,6 +115,18 @@ __device__ __forceinline__ void tc_mma_ta(uint32_t d_tmem, uint32_t a_tmem, uint
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns, waiting until the writes complete.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint4& a, const uint4& b, const uint4& c,
+                                          const uint4& d) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w), "r"(c.x), "r"(c.y), "r"(c.z),
+      "r"(c.w), "r"(d.x), "r"(d.y), "r"(d.z), "r"(d.w)
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // 32 lanes x 8 consecutive 32-bit columns from registers into tensor memory,
@@ -180,8 +199,8 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t word, float s16, float nz
   return r;
 }
 
-template <int XT, int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int XT, int BN, int DW>
+__global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                    const __grid_constant__ CUtensorMap xmap_lo, const __grid_constant__ CUtensorMap omap,
                    const Args a) {
@@ -195,10 +214,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sP = sB + kStages * kBBytes;             // kPStages x 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPStages * kPBytes);
   uint64_t* b_full = bars;                  // [kStages]   TMA(x) -> MMA
-  uint64_t* a_full = b_full + kStages;      // [kStages]   dequant -> MMA (kDeqWarps arrivals)
+  uint64_t* a_full = b_full + kStages;      // [kStages]   dequant -> MMA (DW arrivals)
   uint64_t* empty = a_full + kStages;       // [kStages]   MMA commit -> producers
   uint64_t* p_full = empty + kStages;       // [kPStages]  TMA(packed) -> dequant
-  uint64_t* p_empty = p_full + kPStages;    // [kPStages]  dequant -> TMA(packed) (kDeqWarps arrivals)
+  uint64_t* p_empty = p_full + kPStages;    // [kPStages]  dequant -> TMA(packed) (DW arrivals)
   uint64_t* acc_full = p_empty + kPStages;  // final commit -> epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
@@ -217,12 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&b_full[i], 1);
-      mbar_init(&a_full[i], kDeqWarps);
+      mbar_init(&a_full[i], DW);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < kPStages; ++i) {
       mbar_init(&p_full[i], 1);
-      mbar_init(&p_empty[i], kDeqWarps);
+      mbar_init(&p_empty[i], DW);
     }
     mbar_init(acc_full, 1);
     fence_barrier_init();
@@ -290,10 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(acc_full);
     }
   } else {
-    // ---------------- dequantise (warps 2..17) into tensor memory ----------------
+    // ---------------- dequantise (warps 2..) into tensor memory ----------------
     // A warp may only access the TMEM lanes of its quarter (warp % 4): warp w
-    // dequantises rows 32 (w % 4) + lane, codes 16 sub .. 16 sub + 15 of each
-    // group (sub = (w - 2) / 4), i.e. 8 packed bytes -> 8 TMEM columns.
+    // dequantises rows 32 (w % 4) + lane and, of each group, the codes of
+    // slice sub = (w - 2) / 4: 16 codes (8 packed bytes -> 8 TMEM columns) with
+    // 16 such warps, 32 codes (16 bytes -> 16 columns) with 8.
+    constexpr int kSpan = 16 / DW;  // 16-code slices per thread per group
     const int quarter = warp & 3;
     const int sub = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // tile row 0..127
@@ -323,10 +344,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         nz4[j] = (row_ok && kn < KT) ? load_zero(a.zeros, zrow + kn) : 0;
       }
       mbar_wait(&p_full[p], pph, &g_gemm_tc_error);
-      uint2 q[4];
+      uint4 q[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        q[j] = lds64(sP_addr + p * kPBytes + r * 128 + (((j * 2 + (sub >> 1)) ^ (r & 7)) << 4) + ((sub & 1) << 3));
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (kSpan == 1) {
+          const uint2 h =
+              lds64(sP_addr + p * kPBytes + r * 128 + (((j * 2 + (sub >> 1)) ^ (r & 7)) << 4) + ((sub & 1) << 3));
+          q[j] = make_uint4(h.x, h.y, 0u, 0u);
+        } else {  // slices 2 sub and 2 sub + 1: the whole 16-byte chunk j * 2 + sub
+          q[j] = lds128(sP_addr + p * kPBytes + r * 128 + (((j * 2 + sub) ^ (r & 7)) << 4));
+        }
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_empty[p]);  // box consumed into registers
 #pragma unroll
@@ -338,9 +366,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float s16 = 16.0f * sc4[j], nz = -static_cast<float>(24 + z4[j]) * sc4[j];
         const uint4 d0 = dequant_word<XT>(q[j].x, s16, nz);
         const uint4 d1 = dequant_word<XT>(q[j].y, s16, nz);
-        mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
-        tc_fence_after();
-        tmem_st8(tmem_a + t_lane + (uint32_t)(32 * s + 8 * sub), d0, d1);
+        if constexpr (kSpan == 1) {
+          mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
+          tc_fence_after();
+          tmem_st8(tmem_a + t_lane + (uint32_t)(32 * s + 8 * sub), d0, d1);
+        } else {
+          const uint4 d2 = dequant_word<XT>(q[j].z, s16, nz);
+          const uint4 d3 = dequant_word<XT>(q[j].w, s16, nz);
+          mbar_wait(&empty[s], ph ^ 1u, &g_gemm_tc_error);
+          tc_fence_after();
+          tmem_st16(tmem_a + t_lane + (uint32_t)(32 * s + 16 * sub), d0, d1, d2, d3);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[s]);
@@ -355,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue ----------------
     mbar_wait(acc_full, 0, &g_gemm_tc_error);
     tc_fence_after();
-    constexpr int kSlices = kDeqWarps / 4;                         // warps per lane quarter
+    constexpr int kSlices = DW / 4;                                // warps per lane quarter
     constexpr int kCols = BN / kSlices >= 32 ? BN / kSlices : 32;  // columns per warp (TMEM loads are x32)
     const int er = quarter * 32 + lane;                            // tile row of this thread
     const int64_t orow = n0 + er;
@@ -391,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (a.tma_out) {
       fence_proxy_async_smem();  // staged tile -> visible to the TMA engine
-      asm volatile("bar.sync 1, %0;" ::"r"(32 * kDeqWarps) : "memory");  // the dequant/epilogue warps only
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * DW) : "memory");  // the dequant/epilogue warps only
       if (warp == 2 && lane == 0) {
         tma_store_2d(&omap, (int)n0, m0, sB);
         tma_store_commit_and_wait();
@@ -410,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int per = (kTileN + nranks - 1) / nranks;
       const int rlo = (int)cluster.block_rank() * per;
       const int rows = min(kTileN, rlo + per) - rlo;
-      for (int i = (int)threadIdx.x - 64; rows > 0 && i < rows * BN; i += 32 * kDeqWarps) {
+      for (int i = (int)threadIdx.x - 64; rows > 0 && i < rows * BN; i += 32 * DW) {
         const int c = i / rows, r = rlo + (i - c * rows);
         float sum = 0.f;
         for (int q = 0; q < nranks; ++q) sum += cluster.map_shared_rank(part, q)[c * kTileN + r];
@@ -440,11 +476,11 @@ size_t smem_bytes(int BN, int x_tiles, int ksplit) {
          (ksplit > 1 ? (size_t)BN * kTileN * sizeof(float) : 0);
 }
 
-template <int XT, int BN>
+template <int XT, int BN, int DW>
 cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                       const CUtensorMap& omap, const Args& a, cudaStream_t stream, bool pdl) {
   const size_t smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1, a.ksplit);
-  auto kernel = gemm_tc_kernel<XT, BN>;
+  auto kernel = gemm_tc_kernel<XT, BN, DW>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -458,7 +494,7 @@ cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CU
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), (unsigned)a.ksplit);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(gemm_threads(DW), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
@@ -484,11 +520,15 @@ template <int XT>
 cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                      const CUtensorMap& omap, const Args& a, cudaStream_t s, bool pdl) {
   switch (a.BN) {
-    case 64: return launch_bn<XT, 64>(wmap, xmap, xmap_lo, omap, a, s, pdl);
-    case 128: return launch_bn<XT, 128>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 64:
+      return a.dw == 8 ? launch_bn<XT, 64, 8>(wmap, xmap, xmap_lo, omap, a, s, pdl)
+                       : launch_bn<XT, 64, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 128:
+      return a.dw == 8 ? launch_bn<XT, 128, 8>(wmap, xmap, xmap_lo, omap, a, s, pdl)
+                       : launch_bn<XT, 128, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
     default:
       if constexpr (XT == QI4_DTYPE_F32) return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
-      else return launch_bn<XT, 256>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+      else return launch_bn<XT, 256, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
   }
 }
 
@@ -567,6 +607,9 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
       }
     }
   }
+  // 16 dequantise warps, one CTA per SM: measured faster at M = 2048 than
+  // 128-token tiles with 8 warps and two CTAs per SM (700 vs 595 TFLOP/s).
+  a.dw = 16;
   plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&xmap_lo, 0, sizeof(xmap_lo));
@@ -676,6 +719,7 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
   a.out = out;
   a.out_dtype = QI4_DTYPE_F32;
   a.BN = M > 64 ? 128 : 64;
+  a.dw = 16;
   plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&omap, 0, sizeof(omap));
