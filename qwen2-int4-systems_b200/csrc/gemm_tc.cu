@@ -78,7 +78,7 @@ struct Args {
   int out_dtype;
   int BN;
   int tma_out;  // 1: output tile staged in shared memory and written by one TMA store
-  int dw;       // dequantise/epilogue warps per CTA: 16 or 8 (two CTAs per SM, BN <= 128)
+  int dw;       // dequantise/epilogue warps per CTA (16; the kernel also compiles for 8)
   int ksplit;   // CTAs per cluster along K (grid z); > 1 reduces FP32 partial tiles over DSMEM
   int bps;      // packed 128-byte boxes (4 groups) per K split
 };
@@ -520,12 +520,8 @@ template <int XT>
 cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                      const CUtensorMap& omap, const Args& a, cudaStream_t s, bool pdl) {
   switch (a.BN) {
-    case 64:
-      return a.dw == 8 ? launch_bn<XT, 64, 8>(wmap, xmap, xmap_lo, omap, a, s, pdl)
-                       : launch_bn<XT, 64, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
-    case 128:
-      return a.dw == 8 ? launch_bn<XT, 128, 8>(wmap, xmap, xmap_lo, omap, a, s, pdl)
-                       : launch_bn<XT, 128, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 64: return launch_bn<XT, 64, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 128: return launch_bn<XT, 128, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
     default:
       if constexpr (XT == QI4_DTYPE_F32) return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
       else return launch_bn<XT, 256, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
