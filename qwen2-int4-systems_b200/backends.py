@@ -59,8 +59,21 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# Host cost matters here: the model calls the linear ~200 times per decoded
+# token. torch's raw accessors for the current device and stream skip the
+# Python wrappers of torch.cuda.current_stream / current_device.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_raw_device = getattr(torch._C, "_cuda_getDevice", None)
+
+
 def _stream(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _current_device() -> int:
+    return _raw_device() if _raw_device is not None else torch.cuda.current_device()
 
 
 def _aligned(t: torch.Tensor, n: int = 16) -> torch.Tensor:
@@ -71,14 +84,20 @@ def _aligned(t: torch.Tensor, n: int = 16) -> torch.Tensor:
     return t
 
 
+_cuda_seen = False
+
+
 def _require_cuda():
-    if not torch.cuda.is_available():
-        raise RuntimeError("B200 backend requires a CUDA device; there is no CPU fallback")
+    global _cuda_seen
+    if not _cuda_seen:  # once a device was seen it stays (torch.cuda.is_available reads the environment)
+        if not torch.cuda.is_available():
+            raise RuntimeError("B200 backend requires a CUDA device; there is no CPU fallback")
+        _cuda_seen = True
     return _lib.load()
 
 
 def _validate_linear(x, qweight, scales, zeros, bias, out_features, in_features, group_size, packing):
-    if _packing_value(packing) != "canonical":
+    if packing != "canonical" and _packing_value(packing) != "canonical":
         raise ValueError("B200 backend supports only canonical INT4 packing")
     if group_size != GROUP_SIZE:
         raise ValueError("B200 backend supports only canonical W4G64 tensors")
@@ -97,23 +116,26 @@ def _validate_linear(x, qweight, scales, zeros, bias, out_features, in_features,
     expected_zero = (out_features * groups + 1) // 2
     if qweight.numel() != expected_weight:
         raise ValueError(f"qweight must contain {expected_weight} bytes, got {qweight.numel()}")
-    if tuple(scales.shape) != (out_features, groups):
+    if scales.shape != (out_features, groups):
         raise ValueError(f"scales must have shape {(out_features, groups)}, got {tuple(scales.shape)}")
     if zeros.numel() != expected_zero:
         raise ValueError(f"zeros must contain {expected_zero} bytes, got {zeros.numel()}")
     if bias is not None:
-        if tuple(bias.shape) != (out_features,):
+        if bias.shape != (out_features,):
             raise ValueError(f"bias must have shape {(out_features,)}, got {tuple(bias.shape)}")
         if bias.dtype not in _DTYPE_CODE:
             raise TypeError("bias must use FP16, BF16, or FP32")
-    tensors = (x, qweight, scales, zeros) + (() if bias is None else (bias,))
-    if any(t.device.type != "cuda" for t in tensors):
+    if not (x.is_cuda and qweight.is_cuda and scales.is_cuda and zeros.is_cuda and (bias is None or bias.is_cuda)):
         raise ValueError("B200 backend inputs must be CUDA tensors")
-    if any(t.device != x.device for t in tensors):
+    d = x.get_device()
+    if (qweight.get_device() != d or scales.get_device() != d or zeros.get_device() != d
+            or (bias is not None and bias.get_device() != d)):
         raise ValueError("all B200 backend inputs must be on the same device")
-    for name, t in (("qweight", qweight), ("scales", scales), ("zeros", zeros), ("bias", bias)):
-        if t is not None and not t.is_contiguous():
-            raise ValueError(f"{name} must be contiguous")
+    if not (qweight.is_contiguous() and scales.is_contiguous() and zeros.is_contiguous()
+            and (bias is None or bias.is_contiguous())):
+        for name, t in (("qweight", qweight), ("scales", scales), ("zeros", zeros), ("bias", bias)):
+            if t is not None and not t.is_contiguous():
+                raise ValueError(f"{name} must be contiguous")
     if _value_checks:
         if not torch.isfinite(scales).all() or torch.any(scales <= 0):
             raise ValueError("canonical group scales must be finite and strictly positive")
@@ -124,7 +146,7 @@ def _validate_linear(x, qweight, scales, zeros, bias, out_features, in_features,
 def _launch_linear(x2, qweight, scales, zeros, bias, out, n, algo, pdl):
     lib = _lib.load()
     device = x2.device
-    if torch.cuda.current_device() != device.index:
+    if _current_device() != device.index:
         with torch.cuda.device(device):
             return _launch_linear(x2, qweight, scales, zeros, bias, out, n, algo, pdl)
     if qweight.data_ptr() % 16:
@@ -194,7 +216,7 @@ def b200_w4g64_linear_multi(x: torch.Tensor, layers) -> list[torch.Tensor]:
     outs = [torch.empty((x2.shape[0], l.out_features), dtype=x.dtype, device=x.device) for l in layers]
     if x2.shape[0]:
         device = x2.device
-        if torch.cuda.current_device() != device.index:
+        if _current_device() != device.index:
             with torch.cuda.device(device):
                 return b200_w4g64_linear_multi(x, layers)
         if any(l.qweight.data_ptr() % 16 for l in layers):
@@ -232,7 +254,7 @@ def b200_w4g64_gate_up_silu(x: torch.Tensor, gate_proj, up_proj) -> torch.Tensor
     out = torch.empty((x2.shape[0], n), dtype=torch.float32, device=x.device)
     if x2.shape[0]:
         device = x2.device
-        if torch.cuda.current_device() != device.index:
+        if _current_device() != device.index:
             with torch.cuda.device(device):
                 return b200_w4g64_gate_up_silu(x, gate_proj, up_proj)
         if gate_proj.qweight.data_ptr() % 16 or up_proj.qweight.data_ptr() % 16:
