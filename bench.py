@@ -345,7 +345,9 @@ def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
     """the reference's Qwen2-1.5B (random init, W4G64 RTN) on
     the b200 backend, batch 1, greedy decode through the reference's own
     ``greedy_generate_cached``; the same model on the reference's ``torch``
-    backend on this GPU for comparison (fewer steps)."""
+    backend on this GPU for comparison (fewer steps). The ``b200_fused_mlp``
+    leg also routes the MLP through the fused gate/up SwiGLU call
+    (``register_with_reference(fuse_mlp=True)``)."""
     q2 = importlib.import_module(PACKAGE + ".qwen2")
     try:
         q2.reference_package()
@@ -371,16 +373,20 @@ def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
     cudnn_sdp = torch.backends.cuda.cudnn_sdp_enabled()
     torch.backends.cuda.enable_cudnn_sdp(False)
     with torch.inference_mode():
-        for backend, steps in (("b200", new_tokens), ("torch", 8)):
+        for leg, backend, fuse, steps in (("b200", "b200", False, new_tokens),
+                                          ("b200_fused_mlp", "b200", True, new_tokens),
+                                          ("torch", "torch", False, 8)):
+            q2.register_with_reference(q2.reference_package().__name__, fuse_mlp=fuse)
             model.set_backend(backend)
             gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=3)  # warm-up at full length
             prefill_ms, _ = timed(lambda: model(prompt, use_cache=True))
             total_ms, _ = timed(lambda: gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=steps))
             decode_ms = max(total_ms - prefill_ms, 1e-6)
-            result[backend] = {"prefill_ms": prefill_ms, "new_tokens": steps,
+            result[leg] = {"prefill_ms": prefill_ms, "new_tokens": steps,
                                "generate_ms": total_ms, "decode_tok_s": steps / (decode_ms / 1e3)}
     torch.backends.cuda.enable_cudnn_sdp(cudnn_sdp)
     result["decode_tok_s"] = result["b200"]["decode_tok_s"]
+    result["decode_tok_s_fused_mlp"] = result["b200_fused_mlp"]["decode_tok_s"]
     del model
     torch.cuda.empty_cache()
     return result

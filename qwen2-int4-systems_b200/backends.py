@@ -210,7 +210,8 @@ def b200_w4g64_linear_multi(x: torch.Tensor, layers) -> list[torch.Tensor]:
     if len({b.dtype for b in biases if b is not None}) > 1:
         raise TypeError("grouped linears must share one bias dtype")
     for l, b in zip(layers, biases):
-        _validate_linear(x, l.qweight, l.scales, l.zeros, b, l.out_features, k, GROUP_SIZE, "canonical")
+        _validate_linear(x, l.qweight, l.scales, l.zeros, b, l.out_features, k,
+                         getattr(l, "group_size", GROUP_SIZE), getattr(l, "packing", "canonical"))
     lib = _require_cuda()
     x2 = _aligned(x.reshape(-1, k))
     outs = [torch.empty((x2.shape[0], l.out_features), dtype=x.dtype, device=x.device) for l in layers]
@@ -248,7 +249,8 @@ def b200_w4g64_gate_up_silu(x: torch.Tensor, gate_proj, up_proj) -> torch.Tensor
     if getattr(gate_proj, "bias", None) is not None or getattr(up_proj, "bias", None) is not None:
         raise ValueError("the fused gate/up call takes projections without bias")
     for l in (gate_proj, up_proj):
-        _validate_linear(x, l.qweight, l.scales, l.zeros, None, n, k, GROUP_SIZE, "canonical")
+        _validate_linear(x, l.qweight, l.scales, l.zeros, None, n, k,
+                         getattr(l, "group_size", GROUP_SIZE), getattr(l, "packing", "canonical"))
     lib = _require_cuda()
     x2 = _aligned(x.reshape(-1, k))
     out = torch.empty((x2.shape[0], n), dtype=torch.float32, device=x.device)

@@ -7,20 +7,36 @@ src/qwen_int4/cli.py:59 ``--backend`` choices). ``register_with_reference``
 adds ``"b200"`` to those tables in an already-imported ``qwen_int4`` package,
 so the unmodified model (src/qwen_int4/model.py) runs on the B200 kernels
 after ``model.set_backend("b200")``. The static patch a maintainer would
-commit instead is the three-line change shown in INTEGRATION.md.
+commit instead is a three-line change to those tables.
+
+``fuse_mlp=True`` also routes ``QwenMLP.forward`` (src/qwen_int4/model.py:
+133-136) through the fused gate/up SwiGLU call when both projections are on
+the ``b200`` backend: one launch computes ``silu(gate(x)) * up(x)`` (each
+projection rounded to ``x.dtype`` first, as QuantLinear returns it) in FP32,
+which ``down_proj`` consumes exactly as the reference MLP passes it.
 """
 
 from __future__ import annotations
 
 import importlib
+import sys
 
-from .backends import b200_w4g64_linear
+from .backends import b200_w4g64_gate_up_silu, b200_w4g64_linear
 
 BACKEND = "b200"
 
 
-def register_with_reference(package: str = "qwen_int4") -> None:
-    """Make ``backend="b200"`` valid in the reference's QuantLinear. Idempotent."""
+def register_with_reference(package: str = "qwen_int4", *, fuse_mlp: bool = False) -> None:
+    """Make ``backend="b200"`` valid in the reference's QuantLinear. Idempotent.
+
+    ``fuse_mlp`` selects whether the reference MLP uses the fused gate/up
+    SwiGLU call on that backend; each call sets it (default off).
+    """
+    _register_linear(package)
+    _set_mlp_fusion(package, fuse_mlp)
+
+
+def _register_linear(package: str) -> None:
     backends = importlib.import_module(f"{package}.backends")
     linear = importlib.import_module(f"{package}.linear")
     if BACKEND not in backends.SUPPORTED_BACKENDS:
@@ -44,3 +60,24 @@ def register_with_reference(package: str = "qwen_int4") -> None:
 
     forward._b200_dispatch = True
     quant_linear.forward = forward
+
+
+def _set_mlp_fusion(package: str, enabled: bool) -> None:
+    name = f"{package}.model"
+    if not enabled and name not in sys.modules:
+        return
+    mlp = importlib.import_module(name).QwenMLP
+    if not getattr(mlp.forward, "_b200_fused", False):
+        if not enabled:
+            return
+        reference_forward = mlp.forward
+
+        def forward(self, x):
+            gate, up = self.gate_proj, self.up_proj
+            if type(self)._b200_fuse_mlp and gate.backend == BACKEND and up.backend == BACKEND:
+                return self.down_proj(b200_w4g64_gate_up_silu(x, gate, up)).to(x.dtype)
+            return reference_forward(self, x)
+
+        forward._b200_fused = True
+        mlp.forward = forward
+    mlp._b200_fuse_mlp = enabled

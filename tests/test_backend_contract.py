@@ -6,6 +6,7 @@ tests/test_triton_unpack.py:319-326,345-360,392-400): every bad input raises
 before any launch, with the same error class and message fragment.
 """
 
+import importlib
 import sys
 import types
 
@@ -160,6 +161,48 @@ def test_register_with_reference_adds_explicit_backend(b200):
         assert layer.backend == "b200"
         with pytest.raises(ValueError):
             layer.set_backend("b201")
+    finally:
+        for key in [k for k in sys.modules if k.startswith(name)]:
+            del sys.modules[key]
+
+
+def test_fuse_mlp_switch_routes_only_b200_projections(b200, monkeypatch):
+    """``fuse_mlp`` patches the reference MLP (model.py:133-136): on the b200
+    backend the fused call feeds down_proj; on other backends, or with the
+    switch off again, the reference forward runs unchanged."""
+    integration = importlib.import_module(b200.__name__ + ".integration")
+    name = "fake_qwen_int4_for_mlp_fusion"
+    backends, linear = _fake_reference_package(name)
+    model = types.ModuleType(name + ".model")
+    calls = []
+
+    class QwenMLP(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.gate_proj, self.up_proj = linear.QuantLinear(), linear.QuantLinear()
+            self.down_proj = lambda h: h * 2  # FP32 in, FP32 out
+
+        def forward(self, x):
+            return "reference"
+
+    model.QwenMLP = QwenMLP
+    sys.modules[name + ".model"] = model
+    monkeypatch.setattr(integration, "b200_w4g64_gate_up_silu",
+                        lambda x, g, u: calls.append((g, u)) or torch.ones(2, dtype=torch.float32))
+    try:
+        b200.register_with_reference(name, fuse_mlp=True)
+        mlp = QwenMLP()
+        x = torch.zeros(2, dtype=torch.bfloat16)
+        assert mlp(x) == "reference"  # torch backend: untouched
+        mlp.gate_proj.set_backend("b200")
+        assert mlp(x) == "reference"  # only one projection on b200
+        mlp.up_proj.set_backend("b200")
+        b200.register_with_reference(name, fuse_mlp=True)  # idempotent
+        out = mlp(x)
+        assert calls == [(mlp.gate_proj, mlp.up_proj)]
+        assert out.dtype == torch.bfloat16 and out.tolist() == [2.0, 2.0]
+        b200.register_with_reference(name)  # switch off
+        assert mlp(x) == "reference"
     finally:
         for key in [k for k in sys.modules if k.startswith(name)]:
             del sys.modules[key]

@@ -112,3 +112,33 @@ def test_full_qwen2_greedy_generation_agrees_with_torch_backend(q2, cuda_device)
     assert clear.sum() >= 4
     agree = ref_logits.argmax(-1) == our_logits.argmax(-1)
     assert bool(agree[clear].all()), (agree, clear)
+
+
+def test_fused_mlp_model_matches_torch_backend(q2, cuda_device):
+    """``register_with_reference(fuse_mlp=True)``: every QwenMLP runs the fused
+    gate/up SwiGLU call then down_proj. Cached decode still agrees with the
+    full forward, and the full model's final logits stay within the unfused
+    gate against the reference's torch backend."""
+    cfg = q2.qwen2_config(num_hidden_layers=2, vocab_size=512)
+    small = q2.build_random_qwen2(cfg, device=cuda_device, seed=3, fuse_mlp=True)
+    tokens = torch.randint(0, 512, (2, 9), generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    try:
+        with torch.inference_mode():
+            full = small(tokens)
+            pre, cache = small(tokens[:, :6], use_cache=True)
+            logits, cache = small(tokens[:, 6:7], past_key_values=cache, use_cache=True)
+        assert _cos(pre[:, -1], full[:, 5]) > 0.9999
+        assert _cos(logits[:, -1], full[:, 6]) > 0.9999
+
+        model = q2.build_random_qwen2(device=cuda_device, seed=0, fuse_mlp=True)
+        prompt = torch.randint(0, model.config.vocab_size, (1, 16),
+                               generator=torch.Generator().manual_seed(20260831)).to(cuda_device)
+        with torch.inference_mode():
+            fused = model(prompt)
+            model.set_backend("torch")
+            ref = model(prompt)
+        cos = _cos(fused[0, -1], ref[0, -1])
+        print(f"logits cosine b200 fused MLP vs torch {cos:.6f}")
+        assert cos >= 0.9995
+    finally:
+        q2.register_with_reference(q2.reference_package().__name__, fuse_mlp=False)
