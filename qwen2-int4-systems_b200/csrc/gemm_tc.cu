@@ -205,7 +205,9 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
                    const __grid_constant__ CUtensorMap xmap_lo, const __grid_constant__ CUtensorMap omap,
                    const Args a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offset from the shared array itself (not an integer round trip), so that
+  // every pointer derived from it stays in the shared address space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   // FP32 activations arrive as two bf16 tiles (x = hi + lo), loaded together.
   constexpr int kXTiles = XT == QI4_DTYPE_F32 ? 2 : 1;
   constexpr int kBBytes = kXTiles * BN * 128;       // BN rows x 64 elements (2 bytes), per tile

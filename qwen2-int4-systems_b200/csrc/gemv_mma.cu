@@ -202,7 +202,7 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
   if (XT != QI4_DTYPE_F32 && total <= nthreads) {
     // One chunk per thread at most: load, permute, store.
     if (tid < total) {
-      const int tok = tid / per_tok, c = tid - tok * per_tok;
+      const int tok = a.M == 1 ? 0 : tid / per_tok, c = tid - tok * per_tok;
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(a.x) +
                                                            (int64_t)tok * a.K + (int64_t)g0 * kGroup + c * 8));
       sts128(base + tok * xstride + c * 16,
@@ -234,13 +234,13 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
     // Asynchronous 16-byte copies straight into place (all in flight at
     // once), then each thread permutes the chunks it copied.
     for (int i = tid; i < total; i += nthreads) {
-      const int tok = i / per_tok, c = i - tok * per_tok;
+      const int tok = a.M == 1 ? 0 : i / per_tok, c = i - tok * per_tok;
       cp_async16(base + tok * xstride + c * 16,
                  static_cast<const unsigned short*>(a.x) + (int64_t)tok * a.K + (int64_t)g0 * kGroup + c * 8);
     }
     cp_async_wait_all();
     for (int i = tid; i < total; i += nthreads) {
-      const int tok = i / per_tok, c = i - tok * per_tok;
+      const int tok = a.M == 1 ? 0 : i / per_tok, c = i - tok * per_tok;
       const uint32_t at = base + tok * xstride + c * 16;
       const uint4 v = lds128(at);
       sts128(at, make_uint4(prmt_lo(v.x, v.z), prmt_hi(v.x, v.z), prmt_lo(v.y, v.w), prmt_hi(v.y, v.w)));
@@ -249,7 +249,7 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
     // FP32: through registers (bf16 hi and lo planes), several loads in flight.
 #pragma unroll 4
     for (int i = tid; i < total; i += nthreads) {
-      const int tok = i / per_tok, c = i - tok * per_tok;
+      const int tok = a.M == 1 ? 0 : i / per_tok, c = i - tok * per_tok;
       const int64_t e = (int64_t)tok * a.K + (int64_t)g0 * kGroup + (int64_t)c * 8;
       const float4 v0 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e));
       const float4 v1 = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + e) + 1);
@@ -360,21 +360,24 @@ __device__ __forceinline__ void wait_prerequisites(int tid) {
 
 // D = (c - z) . x for one group of 64 k and the lane's token tile(s), then
 // acc += scale * D (rows r and r + 8 of the lane; FP32 activations as two
-// MMAs of the bf16 hi and lo planes).
+// MMAs of the bf16 hi and lo planes). x_row[n] is the staged row of the
+// lane's token in tile n; lanes past the last token read the last token's
+// row (no fill, no predicate), and their output columns are never stored.
 template <int XT, int NT>
 __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* al, const uint32_t* ah, float s_lo,
-                                          float s_hi, int g, int gq, int M, uint32_t x_lane, int xstride,
-                                          int gs) {
+                                          float s_hi, int g, const uint32_t (&x_row)[NT], int gs) {
 #pragma unroll
   for (int n = 0; n < NT; ++n) {
-    uint4 xb[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    if (n * 8 + gq < M) {
-      const uint32_t xp = x_lane + (uint32_t)(n * 8 * xstride + g * 128);
+    uint4 xb[4];
+    {
+      const uint32_t xp = x_row[n] + (uint32_t)(g * 128);
       xb[0] = lds128(xp);
       xb[1] = lds128(xp + 16);
       if constexpr (XT == QI4_DTYPE_F32) {
         xb[2] = lds128(xp + gs * 128);
         xb[3] = lds128(xp + gs * 128 + 16);
+      } else {
+        xb[2] = xb[3] = make_uint4(0, 0, 0, 0);
       }
     }
     const uint32_t bh[8] = {xb[0].x, xb[0].y, xb[0].z, xb[0].w, xb[1].x, xb[1].y, xb[1].z, xb[1].w};
@@ -393,8 +396,14 @@ __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* a
   }
 }
 
+// CTAs that must fit on one SM: 16-warp CTAs two (64 registers); the 8-warp,
+// one-token-tile kernel of 16- and 32-bit activations four, so that a 560-CTA
+// grid (gate/up at M = 1) is resident in one wave.
+template <int XT, int NT, int WARPS, int PRE>
+constexpr int kMinBlocks = WARPS == 16 ? 2 : (WARPS == 8 && NT == 1 && PRE == 0 && XT != QI4_DTYPE_F32) ? 4 : 1;
+
 template <int XT, int NT, int WARPS, int PRE, bool SW = false>
-__global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
+__global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const Args a) {
   // PRE > 0: every warp has at most PRE groups, expanded into registers
   // before the dependency wait (single-wave grids, whose CTAs start early).
@@ -404,10 +413,16 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
   constexpr int kThr = WARPS * 32;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms.
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Offset from the shared array itself (not an integer round trip), so that
+  // every pointer derived from it stays in the shared address space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  constexpr int kWarpsLog2 = WARPS == 16 ? 4 : WARPS == 8 ? 3 : WARPS == 4 ? 2 : WARPS == 2 ? 1 : 0;
+  static_assert((1 << kWarpsLog2) == WARPS, "warps per CTA must be a power of two");
   const int R = a.rows;
-  const int RB = R >> 4;      // 16-row blocks
-  const int KP = WARPS / RB;  // warps that share one 16-row block
+  const int rb_log2 = a.rows_log2 - 4;   // R is a power of two, 16 <= R <= 16 WARPS
+  const int RB = R >> 4;                 // 16-row blocks
+  const int kp_log2 = kWarpsLog2 - rb_log2;
+  const int KP = 1 << kp_log2;           // warps that share one 16-row block
   const int nbox_total = (a.G + kGroupsPerBox - 1) / kGroupsPerBox;
   const int box0 = blockIdx.y * a.boxes_per_split;
   const int nbox = max(0, min(a.boxes_per_split, nbox_total - box0));  // 0 only for a CTA past the end
@@ -458,18 +473,27 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
     }
   }
   build_table<XT>(a, mt, SW ? &a.mat[1] : nullptr, table, tstride, row0, g0, gs, tid, kThr);
+  // The bias of the row this thread stores (row tid % R: the thread count is
+  // a multiple of R), read before the dependency wait.
+  float bias_r = 0.f;
+  if (!SW && mt.bias != nullptr && gridDim.y == 1) {
+    const int64_t brow = row0 + (tid & (R - 1));
+    if (brow < mt.N) bias_r = load_as_f32(mt.bias, a.bias_dtype, brow);
+  }
   __syncthreads();  // barriers initialised, table complete
 
   const int warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, tq = lane & 3;  // MMA groupID / thread-in-group
-  const int rb = warp % RB, kp = warp / RB;
-  const int gb = (gs * kp) / KP, ge = (gs * (kp + 1)) / KP;  // this warp's groups
+  const int rb = warp & (RB - 1), kp = warp >> rb_log2;
+  const int gb = (gs * kp) >> kp_log2, ge = (gs * (kp + 1)) >> kp_log2;  // this warp's groups
 
   const int r_lo = rb * 16 + gq;
   // Rows r and r + 8 share r % 8 (the swizzle phase): the lane's 8 bytes of
   // group g sit in 16-byte chunk (2 (g % 4) + tq / 2) XOR (r % 8), half tq % 2.
   const uint32_t a_row = smem_addr(wsm) + r_lo * kBoxBytes + ((tq & 1) << 3);
-  const uint32_t x_lane = smem_addr(xs) + gq * xstride + tq * 32;
+  uint32_t x_row[NT];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) x_row[n] = smem_addr(xs) + min(n * 8 + gq, a.M - 1) * xstride + tq * 32;
   const TableEntry* t_lo = table + r_lo * tstride;
   const TableEntry* t_hi = t_lo + 8 * tstride;
 
@@ -505,7 +529,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < PRE; ++j)
-      if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, gq, a.M, x_lane, xstride, gs);
+      if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, x_row, gs);
   } else {
     wait_prerequisites(tid);  // activations come from the previous kernel
     stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
@@ -518,7 +542,10 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
       // of a warp's groups sit at position kp % 4 of their box, so its
       // swizzled chunk offset is fixed.
       const uint32_t coff = (uint32_t)(((((kp & 3) << 1) | (tq >> 1)) ^ (gq & 7)) << 4);
-      for (int g = kp; g < gs; g += KP) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int g = kp + (j << kp_log2);
+        if (g >= gs) break;
         mbar_wait(bars + ((g >> 2) >> a.copy_log2), 0, &g_gemv_mma_error);
         const uint32_t ap = a_row + (uint32_t)((g >> 2) * R * kBoxBytes) + coff;
         const uint2 wl = lds64(ap);
@@ -529,7 +556,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
         expand_word<XT>(wl.y, el.zc2, al + 4);
         expand_word<XT>(wh.x, eh.zc2, ah);
         expand_word<XT>(wh.y, eh.zc2, ah + 4);
-        mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, gq, a.M, x_lane, xstride, gs);
+        mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, x_row, gs);
       }
     } else {
       uint32_t coff[4];  // 16-byte chunk of group j of a box for this lane (swizzled)
@@ -552,7 +579,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
           expand_word<XT>(wl.y, el.zc2, al + 4);
           expand_word<XT>(wh.x, eh.zc2, ah);
           expand_word<XT>(wh.y, eh.zc2, ah + 4);
-          mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, gq, a.M, x_lane, xstride, gs);
+          mma_group<XT, NT>(acc, al, ah, el.scale, eh.scale, g, x_row, gs);
         }
       }
     }
@@ -603,10 +630,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == 16 ? 2 : 1) gemv_mma_kern
       part[(size_t)r * ld + tok] = sum;
     } else {
       const int64_t row = row0 + r;
-      if (row < mt.N) {
-        const float bv = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, row) : 0.f;
-        store_out<XT>(mt.out, (int64_t)tok * mt.N + row, sum + bv);
-      }
+      if (row < mt.N) store_out<XT>(mt.out, (int64_t)tok * mt.N + row, sum + bias_r);
     }
   }
   if (!split) return;
