@@ -108,13 +108,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   if (mbar_try_wait(bar, parity)) return true;
-  // A wait that already timed out somewhere means the pipeline is broken:
-  // give up at once instead of queueing further time-outs.
-  if (*reinterpret_cast<volatile int*>(err) != 0) return false;
   const uint64_t start = global_timer_ns();
   for (;;) {
     for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    // A wait that already timed out somewhere means the pipeline is broken:
+    // give up instead of queueing further time-outs. (Checked here, not
+    // before the first spin, so that an ordinary short wait never pays a
+    // global-memory round trip.)
+    if (*reinterpret_cast<volatile int*>(err) != 0) return false;
     if (global_timer_ns() - start > kWaitLimitNs) break;
   }
   atomicOr(err, kErrWaitTimeout);
