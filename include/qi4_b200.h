@@ -163,6 +163,13 @@ QI4_API int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_
  * counterpart. */
 QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps);
 
+/* Tuning hook: forces the tensor-core GEMM (M > 16) launch shape for
+ * subsequent calls made by the calling thread - tokens per tile (32, 64, 128,
+ * 192 or 256; FP32 activations at most 128) and the K split over a cluster
+ * (1..8; above 1 only for tiles of at most 128 tokens). bn = 0 restores the
+ * library's own choice. No reference counterpart. */
+QI4_API int qi4_gemm_tc_plan_override(int bn, int ksplit);
+
 /* Reports, without touching a GPU, the TMA/tensor-pipe GEMV launch plan the
  * library would use for an M x K activation block, N output features and
  * `num_sms` SMs: plan[0..5] = rows per CTA, K-split factor, warps per CTA,

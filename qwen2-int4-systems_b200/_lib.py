@@ -28,6 +28,7 @@ SIGNATURES = {
     "qi4_w4g64_linear_f32_noalloc": [_p, _i64, _i64, _p, _p, _p, _p, _i, _p, _i64, _p],
     "qi4_gemv_plan_override": [_i, _i, _i, _i],
     "qi4_gemv_mma_plan_override": [_i, _i, _i],
+    "qi4_gemm_tc_plan_override": [_i, _i],
     "qi4_w4g64_linear_multi": [_p, _i, _i64, _i64, _i, _p, _p, _p, _p, _i, _p, _p, _p],
     "qi4_w4g64_gate_up_silu": [_p, _i, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "qi4_gemv_mma_plan": [_i64, _i64, _i64, _i, _i, _p],

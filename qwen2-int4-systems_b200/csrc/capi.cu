@@ -419,6 +419,21 @@ int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int num_sms,
   return QI4_OK;
 }
 
+int qi4_gemm_tc_plan_override(int bn, int ksplit) {
+  clear_error();
+  if (bn == 0) {
+    set_gemm_tc_override(0, 0);
+    return QI4_OK;
+  }
+  if ((bn != 32 && bn != 64 && bn != 128 && bn != 192 && bn != 256) || ksplit < 1 || ksplit > 8 ||
+      (ksplit > 1 && bn > 128)) {
+    set_error("invalid tensor-core GEMM plan override (bn %d, ksplit %d)", bn, ksplit);
+    return QI4_ERR_ARGUMENT;
+  }
+  set_gemm_tc_override(bn, ksplit);
+  return QI4_OK;
+}
+
 int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps) {
   clear_error();
   if (rows == 0) {

@@ -393,8 +393,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     // ---------------- epilogue ----------------
     mbar_wait(acc_full, 0, &g_gemm_tc_error);
     tc_fence_after();
-    constexpr int kSlices = DW / 4;                                // warps per lane quarter
-    constexpr int kCols = BN / kSlices >= 32 ? BN / kSlices : 32;  // columns per warp (TMEM loads are x32)
+    constexpr int kSlices = DW / 4;  // warps per lane quarter; warp `sub` takes 32-column blocks sub, sub + kSlices, ...
     const int er = quarter * 32 + lane;                            // tile row of this thread
     const int64_t orow = n0 + er;
     const float bv = (orow < a.N && a.bias) ? load_as_f32(a.bias, a.bias_dtype, orow) : 0.f;
@@ -403,7 +402,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     uint16_t* sO = reinterpret_cast<uint16_t*>(sB);
     float* sO32 = reinterpret_cast<float*>(sB);
 #pragma unroll 1
-    for (int c0 = sub * kCols; c0 < (sub + 1) * kCols && c0 < BN; c0 += 32) {
+    for (int c0 = sub * 32; c0 < BN; c0 += kSlices * 32) {
       uint32_t v[32];
       tmem_ld32(tmem_d + t_lane + (uint32_t)c0, v);
       if (a.ksplit > 1) {  // partial sums stay in shared memory for the cluster reduction
@@ -522,27 +521,72 @@ template <int XT>
 cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                      const CUtensorMap& omap, const Args& a, cudaStream_t s, bool pdl) {
   switch (a.BN) {
+    case 32: return launch_bn<XT, 32, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
     case 64: return launch_bn<XT, 64, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
     case 128: return launch_bn<XT, 128, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
     default:
-      if constexpr (XT == QI4_DTYPE_F32) return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
-      else return launch_bn<XT, 256, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+      if constexpr (XT == QI4_DTYPE_F32) {
+        return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
+      } else {
+        if (a.BN == 192) return launch_bn<XT, 192, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+        return launch_bn<XT, 256, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+      }
   }
 }
 
-// K split for M <= 128 when the grid is smaller than the SM count (few
-// weight tiles x one token tile, each otherwise running every stage of K in
-// series): up to 8 CTAs per cluster, each at least one packed box (4
-// groups), partial tiles reduced over distributed shared memory. Measured on
-// B200: 1.7x at M = 32, 1.2x at M = 128; at larger M the per-CTA work already
-// hides the pipeline latency and the cluster reduction only costs (k/v at
-// M = 2048 went from 14 to 23 us), so K stays whole there.
-void plan_ksplit(Args& a, int num_sms) {
+thread_local int g_override_bn = 0, g_override_ks = 0;
+
+// Estimated time (microseconds) of a plan: waves of CTAs x per-CTA time, the
+// per-CTA time being its packed boxes (4 groups of K each) x (an MMA cost per
+// token present in the tile plus a per-box dequantisation cost that does not
+// shrink with the tile) plus a fixed pipeline fill, and, when K is split over
+// a cluster, the reduction of the FP32 partial tiles. The constants are a
+// least-squares fit to sweeps on B200 of tile widths 64..256 and splits 1..8
+// over the Qwen2-1.5B shapes at M = 32, 64, 128, 512 and 2048.
+double plan_cost(int64_t M, int64_t N, int nbox, int bn, int ks, int num_sms) {
+  const int bps = (nbox + ks - 1) / ks;
+  ks = (nbox + bps - 1) / bps;
+  const int64_t ctas = ((N + kTileN - 1) / kTileN) * ((M + bn - 1) / bn) * ks;
+  const double waves = (double)((ctas + num_sms - 1) / num_sms);
+  const double tokens = (double)std::min<int64_t>(M, bn);
+  return waves * (bps * (1.619e-3 * tokens + 1.503) + 3.38 + (ks > 1 ? 0.03864 * bn + 2.45 : 0.0));
+}
+
+// Token-tile width and K split: the cheapest plan by plan_cost over widths
+// 256, 128 and 64 (wider tiles need M above half their width; FP32
+// activations, two tiles per stage, at most 128) and clusters of 1, 2, 4 or 8
+// CTAs along K. A split needs partial tiles of at most 128 tokens and
+// M <= 512 (at larger M the per-CTA work already hides the pipeline latency),
+// and its grid at most 0.65 x the SM count: larger cluster grids were
+// measured to run well below the estimate (clusters of one-CTA-per-SM
+// kernels do not pack every SM).
+void plan_tiles(Args& a, int x_dtype, int num_sms) {
   const int nbox = (int)((a.K / kGroup + 3) / 4);
-  const int64_t tiles = ((a.N + kTileN - 1) / kTileN) * ((a.M + a.BN - 1) / a.BN);
-  int ks = 1;
-  if (a.M <= 128 && a.BN <= 128 && tiles < num_sms && nbox >= 2)
-    ks = (int)std::min<int64_t>({8, (int64_t)nbox, (num_sms + tiles - 1) / tiles});
+  const int64_t ntiles = (a.N + kTileN - 1) / kTileN;
+  double best = 1e30;
+  a.BN = 64;
+  int ks_best = 1;
+  for (int bn : {256, 128, 64}) {
+    if (bn > 64 && a.M <= bn / 2) continue;
+    if (bn > 128 && x_dtype == QI4_DTYPE_F32) continue;
+    for (int ks : {1, 2, 4, 8}) {
+      const int bps = (nbox + ks - 1) / ks, kse = (nbox + bps - 1) / bps;
+      if (kse > 1 && (bn > 128 || a.M > 512 ||
+                      (double)(ntiles * ((a.M + bn - 1) / bn) * kse) > 0.65 * num_sms))
+        continue;
+      const double t = plan_cost(a.M, a.N, nbox, bn, ks, num_sms);
+      if (t < best) {
+        best = t;
+        a.BN = bn;
+        ks_best = kse;
+      }
+    }
+  }
+  int ks = ks_best;
+  if (g_override_bn) {
+    a.BN = g_override_bn;
+    ks = a.BN <= 128 ? std::min(g_override_ks, nbox) : 1;
+  }
   a.bps = (nbox + ks - 1) / ks;
   a.ksplit = (nbox + a.bps - 1) / a.bps;  // every CTA of the cluster gets at least one box
 }
@@ -567,6 +611,11 @@ __global__ void __launch_bounds__(256) split_f32_kernel(const float4* __restrict
 
 }  // namespace
 
+void set_gemm_tc_override(int bn, int ksplit) {
+  g_override_bn = bn;
+  g_override_ks = bn ? ksplit : 0;
+}
+
 bool tc_supported(int64_t M, int64_t N, int64_t K, int x_dtype) {
   (void)N;
   return M >= 1 && K >= kGroup && K % kGroup == 0 &&
@@ -586,29 +635,10 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
   a.bias_dtype = bias_dtype;
   a.out = out;
   a.out_dtype = x_dtype;
-  // Token-tile width: tiles per SM x per-tile cost, the per-tile cost being
-  // the MMA time (proportional to BN) plus a dequantisation share that does
-  // not shrink with BN.
-  {
-    const int64_t ntiles = (N + kTileN - 1) / kTileN;
-    double best = 1e30;
-    a.BN = 64;
-    for (int bn : {256, 128, 64}) {
-      if (bn > 64 && M <= bn / 2) continue;
-      if (bn > 128 && x_dtype == QI4_DTYPE_F32) continue;  // two activation tiles per stage
-      const int64_t ctas = ntiles * ((M + bn - 1) / bn);
-      const double waves = (double)((ctas + num_sms - 1) / num_sms);
-      const double t = waves * (bn + 96.0);
-      if (t < best) {
-        best = t;
-        a.BN = bn;
-      }
-    }
-  }
+  plan_tiles(a, x_dtype, num_sms);
   // 16 dequantise warps, one CTA per SM: measured faster at M = 2048 than
   // 128-token tiles with 8 warps and two CTAs per SM (700 vs 595 TFLOP/s).
   a.dw = 16;
-  plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&xmap_lo, 0, sizeof(xmap_lo));
   memset(&omap, 0, sizeof(omap));
@@ -716,9 +746,8 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
   a.bias_dtype = bias_dtype;
   a.out = out;
   a.out_dtype = QI4_DTYPE_F32;
-  a.BN = M > 64 ? 128 : 64;
+  plan_tiles(a, QI4_DTYPE_F32, num_sms);
   a.dw = 16;
-  plan_ksplit(a, num_sms);
   CUtensorMap wmap, xmap, xmap_lo, omap;
   memset(&omap, 0, sizeof(omap));
   // Every element of the hi / lo arrays that the GEMM reads is written by the

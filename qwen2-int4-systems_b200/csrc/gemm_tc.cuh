@@ -21,6 +21,11 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
                                       const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype,
                                       float* out, int64_t N, cudaStream_t stream, int num_sms);
 
+// Forces the token-tile width (32, 64, 128, 192 or 256; FP32 activations at
+// most 128) and the K split (1..8, tiles of at most 128 tokens) of later
+// launches from the calling thread; bn = 0 restores the library's choice.
+void set_gemm_tc_override(int bn, int ksplit);
+
 // Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
 int read_gemm_tc_error(cudaStream_t stream);
 
