@@ -112,3 +112,16 @@ def test_gemv_planner_honours_and_validates_overrides(b200):
         lib.qi4_gemv_mma_plan_override(0, 0, 0)
     for bad in ((24, 1, 4), (16, 0, 4), (16, 9, 4), (16, 1, 3), (64, 1, 2)):
         assert lib.qi4_gemv_mma_plan_override(*bad) == -1
+
+
+def test_gemm_override_validates_without_a_gpu(b200):
+    """qi4_gemm_tc_plan_override: token-tile widths 32/64/128/192/256, K split
+    1..8 only for tiles of at most 128 tokens; bn = 0 restores the planner."""
+    _, lib = _lib(b200)
+    try:
+        for ok in ((32, 1), (64, 8), (128, 2), (192, 1), (256, 1), (0, 0)):
+            assert lib.qi4_gemm_tc_plan_override(*ok) == 0, ok
+        for bad in ((96, 1), (64, 0), (64, 9), (192, 2), (256, 4), (-1, 1)):
+            assert lib.qi4_gemm_tc_plan_override(*bad) == -1, bad
+    finally:
+        lib.qi4_gemm_tc_plan_override(0, 0)
