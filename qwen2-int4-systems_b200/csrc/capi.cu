@@ -66,6 +66,38 @@ int current_device(DeviceInfo& info) {
 
 }  // namespace
 
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!pools[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      e = cudaMemPoolCreate(&pools[dev], &props);
+      if (e != cudaSuccess) {
+        pools[dev] = nullptr;
+        return e;
+      }
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pool = pools[dev];
+  }
+  return cudaMallocFromPoolAsync(p, bytes, pool, stream);
+}
+
+void scratch_free(void* p, cudaStream_t stream) {
+  if (p) cudaFreeAsync(p, stream);
+}
+
 void set_error(const char* fmt, ...) {
   char buf[512];
   va_list ap;
@@ -279,7 +311,7 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
   const size_t bytes = (size_t)M * (size_t)N * xsize;
   const size_t half = (bytes + 255) / 256 * 256;
   void* scratch = nullptr;
-  if (cudaMallocAsync(&scratch, 2 * half, stream) != cudaSuccess) {
+  if (scratch_alloc(&scratch, 2 * half, stream) != cudaSuccess) {
     set_error("scratch allocation of %zu bytes failed", 2 * half);
     return QI4_ERR_DEVICE;
   }
@@ -290,7 +322,7 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
   if (!rc)
     rc = linear_impl(x, x_dtype, M, K, qw_up, sc_up, z_up, nullptr, QI4_DTYPE_NONE, u, N, stream_ptr, QI4_ALGO_AUTO, 1);
   if (!rc) rc = check_launch(launch_swiglu_elementwise(g, u, x_dtype, out, M * N, stream, info.sms), "SwiGLU");
-  cudaFreeAsync(scratch, stream);
+  scratch_free(scratch, stream);
   return rc;
 }
 

@@ -651,7 +651,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
   const void* x_lo = nullptr;
   if (x_dtype == QI4_DTYPE_F32) {
     const size_t half_bytes = (size_t)M * (size_t)K * 2;
-    cudaError_t e = cudaMallocAsync(&scratch, 2 * half_bytes, stream);
+    cudaError_t e = scratch_alloc(&scratch, 2 * half_bytes, stream);
     if (e != cudaSuccess) return e;
     const int64_t n4 = M * K / 4;
     const int blocks = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms * 8);
@@ -683,7 +683,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
         : x_dtype == QI4_DTYPE_F32 ? launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
                                    : launch_x<QI4_DTYPE_BF16>(wmap, xmap, xmap_lo, omap, a, stream, pdl);
   }
-  if (scratch) cudaFreeAsync(scratch, stream);
+  scratch_free(scratch, stream);
   return e;
 }
 
@@ -691,7 +691,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
 // Allocation-free variant of the FP32-activation path
 // ---------------------------------------------------------------------------
 // The FP32-activation path above needs scratch for the bf16 hi/lo copies of
-// x and gets it from cudaMallocAsync. Some callers cannot allocate device
+// x and gets it from the library's scratch pool. Some callers cannot allocate device
 // memory at call time: engines that plan every byte of device memory up
 // front and run under a hard memory cap, hosts that reach this library over a
 // plain C FFI and manage no CUDA allocator of their own, and latency-critical

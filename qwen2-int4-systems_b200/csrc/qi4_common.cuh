@@ -22,6 +22,13 @@ constexpr int kChunkBytes = 16;
 // Host-side error reporting (thread-local message, see qi4_last_error).
 // ---------------------------------------------------------------------------
 void set_error(const char* fmt, ...);
+
+// Stream-ordered scratch from a per-device pool of the library that keeps
+// freed memory for reuse (release threshold at its maximum): repeated calls
+// do not map fresh device memory each time the device synchronises, as the
+// default pool does. Free with scratch_free on the same stream.
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream);
+void scratch_free(void* p, cudaStream_t stream);
 void clear_error();
 int launch_status(const char* what);  // checks cudaGetLastError after a launch
 
