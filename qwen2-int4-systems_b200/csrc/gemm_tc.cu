@@ -30,7 +30,7 @@
 // boxes through the same pipeline; their FP32 partial tiles are parked in
 // shared memory and summed over distributed shared memory, each CTA finishing
 // 128 / ksplit rows of the tile (+ bias, cast, store).
-// Every mbarrier wait is bounded (tma_util.cuh); no TMA multicast is used.
+// Every mbarrier wait is bounded (tma_util.cuh); every CTA loads its own tiles.
 #include <cooperative_groups.h>
 
 #include <algorithm>

@@ -3,8 +3,8 @@
 // Rules this code keeps (sm_100a):
 //   * every tiled TMA load starts at an inner coordinate that is a multiple of
 //     16 bytes, and the inner box is at most the 128-byte swizzle span;
-//   * no .multicast::cluster form is used anywhere - each CTA loads its own
-//     tiles into its own shared memory;
+//   * no cluster-broadcast form of a copy is used anywhere - each CTA loads
+//     its own tiles into its own shared memory;
 //   * every wait on an mbarrier is bounded; on time-out the kernel records an
 //     error code in a device flag and carries on without the data.
 #pragma once
