@@ -86,6 +86,14 @@ def _aligned(t: torch.Tensor, n: int = 16) -> torch.Tensor:
 
 _cuda_seen = False
 
+# C++ fast path of b200_w4g64_linear (csrc/torch_binding.cpp): the same checks
+# and launch on at::Tensor arguments, calling the C ABI directly. Built with
+# the library; without it the call goes through ctypes to the same kernels.
+try:
+    from . import _qi4_torch as _fast
+except ImportError:
+    _fast = None
+
 
 def _require_cuda():
     global _cuda_seen
@@ -182,6 +190,9 @@ def b200_w4g64_linear(
     and ``pdl`` toggles programmatic dependent launch; both default to the
     library's choice.
     """
+    if (_fast is not None and algo == _lib.ALGO_AUTO and pdl and not _value_checks and group_size == GROUP_SIZE
+            and (packing == "canonical" or _packing_value(packing) == "canonical")):
+        return _fast.linear(x, qweight, scales, zeros, bias, out_features, in_features)
     _validate_linear(x, qweight, scales, zeros, bias, out_features, in_features, group_size, packing)
     _require_cuda()
     x2 = x.reshape(-1, in_features)

@@ -94,6 +94,44 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+def binding_path() -> Path:
+    import sysconfig
+    return PKG / ("_qi4_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_binding(force: bool = False) -> Path:
+    """Compile csrc/torch_binding.cpp (the C++ fast path of the Python
+    QuantLinear call) against this interpreter's torch and libqi4_b200.so,
+    in-tree next to the library. Rebuilt when the source, the C header or the
+    library is newer than the module."""
+    import sysconfig
+
+    import torch
+
+    src = CSRC / "torch_binding.cpp"
+    out = binding_path()
+    deps = [src, ROOT / "include" / "qi4_b200.h", LIB]
+    if not force and out.exists() and out.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return out
+    torch_dir = Path(torch.__file__).resolve().parent
+    cuda_home = Path(nvcc()).resolve().parent.parent
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = [shutil.which("g++") or "g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_qi4_torch", "-DTORCH_API_INCLUDE_EXTENSION_H",
+           "-I", str(torch_dir / "include"), "-I", str(torch_dir / "include" / "torch" / "csrc" / "api" / "include"),
+           "-I", sysconfig.get_paths()["include"], "-I", str(cuda_home / "include"), "-I", str(ROOT / "include"),
+           str(src), "-o", str(out) + ".tmp",
+           "-L", str(torch_dir / "lib"), "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lc10", "-lc10_cuda",
+           "-L", str(PKG), "-lqi4_b200", "-Wl,-rpath,$ORIGIN", "-Wl,-rpath," + str(torch_dir / "lib")]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    (BUILD / "torch_binding.log").write_text(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+    if proc.returncode != 0:
+        raise RuntimeError(f"torch binding build failed:\n{proc.stderr[-4000:]}")
+    os.replace(str(out) + ".tmp", out)
+    return out
+
+
 if __name__ == "__main__":
     path = build(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(path)
+    print(build_torch_binding(force="--force" in sys.argv))

@@ -239,3 +239,50 @@ def test_fused_gate_up_rejects_mismatched_projections_without_a_gpu(b200):
         b200.b200_w4g64_gate_up_silu(x, gate, biased)
     with pytest.raises(ValueError, match="CUDA tensors"):
         b200.b200_w4g64_gate_up_silu(x, gate, gate)
+
+
+def _fast_and_python_errors(b200, *args, **kwargs):
+    """Error type and message from the C++ fast path and from the Python checks."""
+    backends = importlib.import_module(b200.__name__ + ".backends")
+    results = []
+    for use_fast in (True, False):
+        saved = backends._fast
+        if not use_fast:
+            backends._fast = None
+        try:
+            b200.b200_w4g64_linear(*args, **kwargs)
+            results.append(None)
+        except (ValueError, TypeError, RuntimeError) as exc:
+            results.append((type(exc), str(exc)))
+        finally:
+            backends._fast = saved
+    return results
+
+
+def test_fast_path_is_built_and_raises_like_the_python_checks(b200):
+    """The C++ fast path of b200_w4g64_linear (csrc/torch_binding.cpp) is part
+    of the build and rejects every malformed call with the Python wrapper's
+    exception class and message (the reference's validator contract)."""
+    backends = importlib.import_module(b200.__name__ + ".backends")
+    assert backends._fast is not None, "the _qi4_torch fast path was not built"
+    qw, sc, z = _tensors()
+    x = torch.zeros(2, 128, dtype=torch.bfloat16)
+    kw = {"out_features": 6, "in_features": 128, "group_size": GROUP, "packing": "canonical"}
+    cases = [
+        ((x, qw, sc, z, None), kw),  # CPU tensors
+        ((x.int(), qw, sc, z, None), kw),
+        ((torch.zeros(2, 64, dtype=torch.bfloat16), qw, sc, z, None), kw),
+        ((x, qw[:-1], sc, z, None), kw),
+        ((x, qw, sc[:, :1], z, None), kw),
+        ((x, qw, sc.reshape(-1), z, None), kw),
+        ((x, qw, sc, z[:-1], None), kw),
+        ((x, qw, sc.float(), z, None), kw),
+        ((x, qw.to(torch.int8), sc, z, None), kw),
+        ((x, qw, sc, z, torch.zeros(5, dtype=torch.bfloat16)), kw),
+        ((x, qw, sc, z, torch.zeros(6, dtype=torch.int32)), kw),
+        ((x, qw, sc, z, None), dict(kw, out_features=0)),
+        ((x, qw, sc, z, None), dict(kw, in_features=96)),
+    ]
+    for args, kwargs in cases:
+        fast, python = _fast_and_python_errors(b200, *args, **kwargs)
+        assert fast is not None and fast == python, (fast, python)
