@@ -688,11 +688,13 @@ cudaError_t launch_t(const CUtensorMap* maps, const Args& a, int ksplit, cudaStr
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int n = 0;
-  attrs[n].id = cudaLaunchAttributeClusterDimension;
-  attrs[n].val.clusterDim.x = 1;
-  attrs[n].val.clusterDim.y = (unsigned)ksplit;
-  attrs[n].val.clusterDim.z = 1;
-  ++n;
+  if (ksplit > 1) {  // a K split reduces over its cluster; whole-K grids launch without one
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = (unsigned)ksplit;
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
   if (pdl) {
     attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[n].val.programmaticStreamSerializationAllowed = 1;
