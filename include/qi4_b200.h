@@ -158,8 +158,8 @@ QI4_API int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_
 
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
- * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8 or 16,
- * at least rows / 16). rows = 0 restores the library's own choice. No reference
+ * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8, 16 or
+ * 32, at least rows / 16). rows = 0 restores the library's own choice. No reference
  * counterpart. */
 QI4_API int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps);
 

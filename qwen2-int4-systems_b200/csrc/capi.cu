@@ -473,7 +473,7 @@ int qi4_gemv_mma_plan_override(int rows, int ksplit, int warps) {
     return QI4_OK;
   }
   if ((rows != 16 && rows != 32 && rows != 64 && rows != 128) || ksplit < 1 || ksplit > 8 ||
-      (warps != 2 && warps != 4 && warps != 8 && warps != 16) || rows / 16 > warps) {
+      (warps != 2 && warps != 4 && warps != 8 && warps != 16 && warps != 32) || rows / 16 > warps) {
     set_error("invalid GEMV plan override (rows %d, ksplit %d, warps %d)", rows, ksplit, warps);
     return QI4_ERR_ARGUMENT;
   }

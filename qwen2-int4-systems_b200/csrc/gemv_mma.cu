@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
   // Offset from the shared array itself (not an integer round trip), so that
   // every pointer derived from it stays in the shared address space.
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  constexpr int kWarpsLog2 = WARPS == 16 ? 4 : WARPS == 8 ? 3 : WARPS == 4 ? 2 : WARPS == 2 ? 1 : 0;
+  constexpr int kWarpsLog2 = WARPS == 32 ? 5 : WARPS == 16 ? 4 : WARPS == 8 ? 3 : WARPS == 4 ? 2 : WARPS == 2 ? 1 : 0;
   static_assert((1 << kWarpsLog2) == WARPS, "warps per CTA must be a power of two");
   const int R = a.rows;
   const int rb_log2 = a.rows_log2 - 4;   // R is a power of two, 16 <= R <= 16 WARPS
@@ -712,6 +712,7 @@ cudaError_t launch_w(const CUtensorMap* map, const Args& a, int warps, int kspli
     case 2: return launch_t<XT, NT, 2, 0>(map, a, ksplit, s, pdl);
     case 4: return launch_t<XT, NT, 4, 0>(map, a, ksplit, s, pdl);
     case 8: return pre ? launch_t<XT, NT, 8, kPreGroups>(map, a, ksplit, s, pdl) : launch_t<XT, NT, 8, 0>(map, a, ksplit, s, pdl);
+    case 32: return launch_t<XT, NT, 32, 0>(map, a, ksplit, s, pdl);
     default: return launch_t<XT, NT, 16, 0>(map, a, ksplit, s, pdl);
   }
 }

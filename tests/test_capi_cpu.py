@@ -90,7 +90,7 @@ def test_gemv_planner_always_terminates_with_a_valid_plan(b200):
                     assert lib.qi4_gemv_mma_plan(m, n, k, dtype, sms, plan) == 0, (m, n, k, dtype)
                     rows, ks, warps, bps, smem, pre = list(plan)
                     nboxes = (k // 64 + 3) // 4
-                    assert rows in (16, 32, 64, 128) and warps in (2, 4, 8, 16) and rows // 16 <= warps
+                    assert rows in (16, 32, 64, 128) and warps in (2, 4, 8, 16, 32) and rows // 16 <= warps
                     assert 1 <= ks <= 8 and bps * (ks - 1) < nboxes <= bps * ks, (m, n, k, ks, bps)
                     assert smem <= 200 * 1024, (m, n, k, dtype, smem)
                     if pre:  # single wave, at most 4 groups per warp
