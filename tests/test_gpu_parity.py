@@ -12,6 +12,8 @@ Tolerances (stated per the north-star contract):
   atol 0.0625, bf16 rtol 0.02 / atol 0.25).
 """
 
+import importlib
+
 import numpy as np
 import pytest
 import torch
@@ -318,3 +320,33 @@ def test_device_status_clean_after_kernels(b200, cuda_device):
     b200.b200_w4g64_linear(x, to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device), None,
                            out_features=256, in_features=1536, group_size=64, packing="canonical")
     assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("n", [100, 200, 1536])
+@pytest.mark.parametrize("m", [1, 3, 9])
+def test_gemv_output_stores_aligned_and_not(b200, cuda_device, dtype, n, m):
+    """The decode GEMV writes 16-bit outputs of whole, 16-byte-aligned tiles
+    as 16-byte stores and falls back to element stores for a partial last
+    tile, a row pitch that is not a multiple of 8 outputs, or an output
+    pointer off the 16-byte grid (C ABI call into an offset buffer)."""
+    import ctypes
+
+    k = 256
+    qw, sc, z = _weights(k, n, "asym", 5)
+    g = torch.Generator().manual_seed(77 + m)
+    x = torch.randn(m, k, generator=g).to(dtype)
+    ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=n, in_features=k, accumulate="f64")
+    lib = importlib.import_module(b200.__name__ + "._lib").load()
+    xd, qwd, scd, zd = x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device), to_dev(z, cuda_device)
+    code = {torch.bfloat16: 1, torch.float16: 0}[dtype]
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    for offset in (0, 1):  # elements: 0 = aligned buffer, 1 = 2-byte offset
+        buf = torch.full((m * n + 8,), float("nan"), dtype=dtype, device=cuda_device)
+        out = buf[offset:offset + m * n]
+        rc = lib.qi4_w4g64_linear_ex(xd.data_ptr(), code, m, k, qwd.data_ptr(), scd.data_ptr(), zd.data_ptr(),
+                                     None, -1, out.data_ptr(), n, ctypes.c_void_p(stream), 1, 1)
+        torch.cuda.synchronize()
+        assert rc == 0
+        assert_linear_close(out.view(m, n), ref, 1e-3, f"n={n} m={m} offset={offset}")
+        assert torch.isnan(buf[:offset]).all() and torch.isnan(buf[offset + m * n:]).all()
