@@ -653,7 +653,7 @@ def main() -> None:
         e2e_ms = float(t.item())
     e2e = {"value": step_bytes * world / (e2e_ms / 1e3) / 1e9, "unit": UNIT,
            "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
-           "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python, ctypes C-ABI)"}
+           "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python call; C++ binding of the C ABI)"}
 
     split = split_prefill(device, dist, world) if dist else None
 
