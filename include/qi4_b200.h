@@ -186,6 +186,14 @@ QI4_API int qi4_gemv_mma_plan(int64_t M, int64_t N, int64_t K, int x_dtype, int 
 #define QI4_DEVICE_WAIT_TIMEOUT 1
 QI4_API int qi4_device_status(void* stream);
 
+/* Failure-detection self-test: enqueues on `stream` one CTA that waits, with
+ * the same bounded wait the kernels use, on a shared-memory barrier nothing
+ * arrives on. The wait gives up after limit_ns (1 us .. 1 s) and records
+ * QI4_DEVICE_WAIT_TIMEOUT, which the next qi4_device_status reports; the CUDA
+ * context stays usable. Lets an operator check that a lost arrival ends as an
+ * error status rather than a hang. No reference counterpart. */
+QI4_API int qi4_selftest_bounded_wait(uint64_t limit_ns, void* stream);
+
 /* Tuning hook: forces the FP32-FMA decode-GEMV launch shape for subsequent calls made
  * by the calling thread - lanes per weight row (8/16/32), warps per CTA,
  * K-split factor (CTAs per cluster, 1..8) and per-lane load depth (4 or 8).

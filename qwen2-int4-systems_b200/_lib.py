@@ -33,6 +33,7 @@ SIGNATURES = {
     "qi4_w4g64_gate_up_silu": [_p, _i, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "qi4_gemv_mma_plan": [_i64, _i64, _i64, _i, _i, _p],
     "qi4_device_status": [_p],
+    "qi4_selftest_bounded_wait": [ctypes.c_uint64, _p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }

@@ -493,6 +493,19 @@ int qi4_device_status(void* stream) {
   return v;
 }
 
+int qi4_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  clear_error();
+  if (limit_ns < 1000 || limit_ns > 1000000000ull) {
+    set_error("limit_ns must lie in [1 us, 1 s] (got %llu ns)", (unsigned long long)limit_ns);
+    return QI4_ERR_ARGUMENT;
+  }
+  DeviceInfo info;
+  const int rc = current_device(info);
+  if (rc) return rc;
+  return check_launch(launch_bounded_wait_selftest(limit_ns, static_cast<cudaStream_t>(stream)),
+                      "bounded-wait self-test");
+}
+
 int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
                                  const uint16_t* scales_f16, const uint8_t* zeros, const void* bias, int bias_dtype,
                                  float* out, int64_t N, void* stream) {

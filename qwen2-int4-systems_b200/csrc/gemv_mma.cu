@@ -950,6 +950,27 @@ cudaError_t launch_swiglu_elementwise(const void* g, const void* u, int dtype, f
   return cudaGetLastError();
 }
 
+namespace {
+
+// One thread waits, with the kernels' bounded wait, on a shared-memory
+// barrier that nothing ever arrives on: the wait gives up after limit_ns and
+// records the time-out in the same device flag the GEMV kernels use.
+__global__ void __launch_bounds__(32) bounded_wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait_for(&bar, 0, &g_gemv_mma_error, limit_ns);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_bounded_wait_selftest(uint64_t limit_ns, cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 int read_gemv_mma_error(cudaStream_t stream) {
   int v = 0;
   if (cudaMemcpyFromSymbolAsync(&v, g_gemv_mma_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) !=

@@ -46,4 +46,7 @@ cudaError_t launch_swiglu_elementwise(const void* g, const void* u, int dtype, f
 // Reads and clears the kernel's device error flag (synchronises `stream`); -1 on failure.
 int read_gemv_mma_error(cudaStream_t stream);
 
+// One CTA whose bounded mbarrier wait runs out after limit_ns (failure-detection self-test).
+cudaError_t launch_bounded_wait_selftest(uint64_t limit_ns, cudaStream_t stream);
+
 }  // namespace qi4

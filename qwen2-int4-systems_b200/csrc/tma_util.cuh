@@ -105,8 +105,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and sets *err) if the phase did not complete
-// within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// within limit_ns.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (;;) {
@@ -117,10 +117,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     // before the first spin, so that an ordinary short wait never pays a
     // global-memory round trip.)
     if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (global_timer_ns() - start > kWaitLimitNs) break;
+    if (global_timer_ns() - start > limit_ns) break;
   }
   atomicOr(err, kErrWaitTimeout);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+  return mbar_wait_for(bar, parity, err, kWaitLimitNs);
 }
 
 // 2-D tiled bulk tensor load global -> this CTA's shared memory, completing

@@ -125,3 +125,11 @@ def test_gemm_override_validates_without_a_gpu(b200):
             assert lib.qi4_gemm_tc_plan_override(*bad) == -1, bad
     finally:
         lib.qi4_gemm_tc_plan_override(0, 0)
+
+
+def test_bounded_wait_selftest_validates_its_limit_without_a_gpu(b200):
+    """qi4_selftest_bounded_wait takes a wait limit of 1 us .. 1 s and rejects
+    anything else before touching a device."""
+    _, lib = _lib(b200)
+    for bad in (0, 999, 1_000_000_001, 2**63):
+        assert lib.qi4_selftest_bounded_wait(bad, None) == -1

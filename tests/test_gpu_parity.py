@@ -350,3 +350,31 @@ def test_gemv_output_stores_aligned_and_not(b200, cuda_device, dtype, n, m):
         assert rc == 0
         assert_linear_close(out.view(m, n), ref, 1e-3, f"n={n} m={m} offset={offset}")
         assert torch.isnan(buf[:offset]).all() and torch.isnan(buf[offset + m * n:]).all()
+
+
+def test_bounded_wait_runs_out_as_a_status_not_a_hang(b200, cuda_device):
+    """Failure detection without a GPU fault: a wait on a barrier that nothing
+    arrives on ends after its limit (10 ms here) and shows up as
+    QI4_DEVICE_WAIT_TIMEOUT in qi4_device_status; the flag is cleared by the
+    read, and the context still runs a linear correctly afterwards."""
+    import time
+
+    lib = importlib.import_module(b200.__name__ + "._lib").load()
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    assert lib.qi4_device_status(stream) >= 0  # clear leftovers
+    t0 = time.perf_counter()
+    assert lib.qi4_selftest_bounded_wait(10_000_000, stream) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert 0.009 <= waited < 5.0, waited
+    assert lib.qi4_device_status(stream) == 1  # QI4_DEVICE_WAIT_TIMEOUT
+    assert lib.qi4_device_status(stream) == 0  # cleared by the read
+    k, n = 128, 64
+    qw, sc, z = _weights(k, n, "asym", 9)
+    x = torch.randn(2, k, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    got = b200.b200_w4g64_linear(x.to(cuda_device), to_dev(qw, cuda_device), to_dev(sc, cuda_device),
+                                 to_dev(z, cuda_device), None, out_features=n, in_features=k, group_size=64,
+                                 packing="canonical")
+    ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=n, in_features=k, accumulate="f64")
+    assert_linear_close(got, ref, 1e-3, "after the self-test")
+    assert lib.qi4_device_status(stream) == 0
