@@ -397,12 +397,17 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     const int er = quarter * 32 + lane;                            // tile row of this thread
     const int64_t orow = n0 + er;
     const float bv = (orow < a.N && a.bias) ? load_as_f32(a.bias, a.bias_dtype, orow) : 0.f;
-    // Output tile staged as [BN tokens][128 rows] in the activation ring,
-    // which the finished main loop no longer uses.
-    uint16_t* sO = reinterpret_cast<uint16_t*>(sB);
-    float* sO32 = reinterpret_cast<float*>(sB);
+    // Output: each warp stages its 32 rows x 32 tokens of a column block as a
+    // contiguous [32 tokens][32 rows] box in the activation ring (which the
+    // finished main loop no longer uses) and stores it with its own TMA store
+    // at once, so staging, stores and the next block's TMEM loads overlap and
+    // no CTA-wide barrier precedes the stores.
+    constexpr int kOsz = XT == QI4_DTYPE_F32 ? 4 : 2;
 #pragma unroll 1
     for (int c0 = sub * 32; c0 < BN; c0 += kSlices * 32) {
+      uint8_t* box = sB + (size_t)((c0 >> 5) * 4 + quarter) * (32 * 32 * kOsz);
+      uint16_t* sO = reinterpret_cast<uint16_t*>(box);
+      float* sO32 = reinterpret_cast<float*>(box);
       uint32_t v[32];
       tmem_ld32(tmem_d + t_lane + (uint32_t)c0, v);
       if (a.ksplit > 1) {  // partial sums stay in shared memory for the cluster reduction
@@ -413,11 +418,16 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
         for (int j = 0; j < 32; ++j) {
           const float f = __uint_as_float(v[j]) + bv;
           if constexpr (XT == QI4_DTYPE_F32)
-            sO32[(c0 + j) * kTileN + er] = f;
+            sO32[j * 32 + lane] = f;
           else
-            sO[(c0 + j) * kTileN + er] = XT == QI4_DTYPE_F16 ? __half_as_ushort(__float2half_rn(f))
-                                                             : __bfloat16_as_ushort(__float2bfloat16_rn(f));
+            sO[j * 32 + lane] = XT == QI4_DTYPE_F16 ? __half_as_ushort(__float2half_rn(f))
+                                                    : __bfloat16_as_ushort(__float2bfloat16_rn(f));
         }
+        fence_proxy_async_smem();  // this thread's staged values -> visible to the TMA engine
+        __syncwarp();
+        // (a box wholly past the last row or token is not issued; partial boxes are clipped by the TMA)
+        if (lane == 0 && n0 + quarter * 32 < a.N && m0 + c0 < a.M)
+          tma_store_2d(&omap, (int)n0 + quarter * 32, m0 + c0, box);
       } else if (orow < a.N) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -426,14 +436,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
         }
       }
     }
-    if (a.tma_out) {
-      fence_proxy_async_smem();  // staged tile -> visible to the TMA engine
-      asm volatile("bar.sync 1, %0;" ::"r"(32 * DW) : "memory");  // the dequant/epilogue warps only
-      if (warp == 2 && lane == 0) {
-        tma_store_2d(&omap, (int)n0, m0, sB);
-        tma_store_commit_and_wait();
-      }
-    }
+    if (a.tma_out && lane == 0) tma_store_commit_and_wait();  // the staged boxes were read
   }
 
   if (a.ksplit > 1) {
@@ -677,8 +680,7 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
                               x_dtype == QI4_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                               : x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                              (uint64_t)N, (uint64_t)M, (uint64_t)N * osz, kTileN, (uint32_t)a.BN,
-                              CU_TENSOR_MAP_SWIZZLE_NONE);
+                              (uint64_t)N, (uint64_t)M, (uint64_t)N * osz, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     e = x_dtype == QI4_DTYPE_F16   ? launch_x<QI4_DTYPE_F16>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
         : x_dtype == QI4_DTYPE_F32 ? launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
                                    : launch_x<QI4_DTYPE_BF16>(wmap, xmap, xmap_lo, omap, a, stream, pdl);
@@ -768,7 +770,7 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
     return cudaErrorInvalidValue;
   a.tma_out = a.ksplit == 1 && ((N * 4) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
               tensor_map_2d(&omap, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)N, (uint64_t)M,
-                            (uint64_t)N * 4, kTileN, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            (uint64_t)N * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
   return launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, false);
 }
 
