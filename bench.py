@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 W4G64 QuantLinear forward (decode GEMV headline).
 
-Workload (BASELINE config 1 at M=1, i.e. one decode token through every
+Workload (the seven-shape sweep at M=1, i.e. one decode token through every
 quantised linear of Qwen2-1.5B): the seven linear shapes q 1536->1536,
 k/v 1536->256, o 1536->1536, gate/up 1536->8960, down 8960->1536, for each
 of the 28 layers, symmetric W4G64 RTN of bf16 weights ~N(0, 0.02), bf16
@@ -9,7 +9,7 @@ activations ~N(0, 1), q/k/v with bf16 bias. A step is one pass over all 196
 linears; the 655 MB of packed weights per step are far larger than L2, so no
 flush is needed. Synthetic, seeded data (no checkpoint is used).
 
-  value  = algorithmic bytes per step (SURVEY 8d formula) / device time,
+  value  = algorithmic bytes per step (N*K/2 + 2*N*K/64 + 2*M*K + 2*M*N per linear, + 2*N with bias) / device time,
            step captured once in a CUDA graph of C-ABI launches, replayed K times
   e2e    = same metric through the public Python API (b200_w4g64_linear) with
            the step's activations copied host->device and outputs device->host
@@ -342,7 +342,7 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------------------
 
 def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
-    """the reference's Qwen2-1.5B (random init, W4G64 RTN) on
+    """Batch-1 decode: the reference's Qwen2-1.5B (random init, W4G64 RTN) on
     the b200 backend, batch 1, greedy decode through the reference's own
     ``greedy_generate_cached``; the same model on the reference's ``torch``
     backend on this GPU for comparison (fewer steps). The ``b200_fused_mlp``
@@ -393,7 +393,7 @@ def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
 
 
 def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> dict:
-    """one Qwen2-1.5B MLP (gate/up/down) at M tokens with
+    """Column-split prefill: one Qwen2-1.5B MLP (gate/up/down) at M tokens with
     gate/up/down column-split over the ranks and NCCL all-gathers (two per
     MLP). Time is the max over ranks of CUDA-event time per forward."""
     par = importlib.import_module(PACKAGE + ".parallel")
@@ -426,7 +426,7 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
 
 
 def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
-    """Secondary figures for the BASELINE configs the headline does not cover:
+    """Secondary figures for the workloads the headline does not cover:
     config 0 (gate, symmetric, M = 1/4/16), config 1's remaining M points
     (8/32/128/512, seven shapes of four layers), config 2 (AWQ-style
     asymmetric down_proj, M = 1/16/2048) and config 4's batch-64 decode step
@@ -502,7 +502,7 @@ def main() -> None:
     parser.add_argument("--no-gemm", action="store_true")
     parser.add_argument("--no-model", action="store_true", help="skip the Qwen2-1.5B decode tok/s section")
     parser.add_argument("--no-configs", action="store_true",
-                        help="skip the secondary BASELINE config figures (configs 0, 1, 2, 4)")
+                        help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, AWQ down, batch-64 linears)")
     parser.add_argument("--profile-case", choices=["gemv", "gemm"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
                              "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv) or M=2048 (gemm)")

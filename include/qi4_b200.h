@@ -118,7 +118,9 @@ QI4_API int qi4_w4_unpack(const uint8_t* packed, int8_t* out, int64_t elements,
  * call before any stream capture. All calls share the one array: calls that
  * may run at the same time on the GPU (different streams without ordering)
  * race on it. Nothing is carried over between calls - each call writes every
- * scratch byte it reads.
+ * scratch byte it reads. The array's address is cached per device for the
+ * life of the process: after cudaDeviceReset on a device, do not call this
+ * entry point on that device again.
  */
 QI4_API int qi4_w4g64_linear_f32_noalloc(const float* x, int64_t M, int64_t K, const uint8_t* qweight,
                                          const uint16_t* scales_f16, const uint8_t* zeros,

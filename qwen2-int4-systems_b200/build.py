@@ -94,6 +94,42 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+REFERENCE_SRC = Path("/root/reference")
+HARNESS = ROOT / "baseline" / "_ref"
+
+
+def install_reference_harness(source: Path = REFERENCE_SRC, force: bool = False) -> Path | None:
+    """Install the reference project's pure-Python package into ``baseline/_ref``.
+
+    The model-level GPU tests and the bench's decode section run the
+    reference's own ``QwenInt4ForCausalLM`` and generation loop unchanged on
+    the ``b200`` backend; this puts that code where ``qwen2.reference_package``
+    looks for it, so that it travels with the tree to a machine without the
+    reference checkout. ``pip install --no-deps --target`` from a temporary
+    copy (the build writes into its source tree). Returns the target, or None
+    when no reference checkout is present (the files already installed are
+    then used as they are)."""
+    import tempfile
+
+    if not force and (HARNESS / "qwen_int4" / "model.py").exists():
+        return HARNESS
+    if not (source / "src" / "qwen_int4").is_dir():
+        return None
+    with tempfile.TemporaryDirectory() as tmp:
+        copy = Path(tmp) / "reference"
+        shutil.copytree(source, copy, ignore=shutil.ignore_patterns(".git", "__pycache__"))
+        staging = HARNESS.with_name("_ref.tmp")
+        shutil.rmtree(staging, ignore_errors=True)
+        cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+               "--find-links", "/opt/wheelhouse", "--target", str(staging), "-q", str(copy)]
+        proc = subprocess.run(cmd, capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise RuntimeError(f"reference harness install failed:\n{proc.stdout}{proc.stderr}")
+    shutil.rmtree(HARNESS, ignore_errors=True)
+    os.replace(staging, HARNESS)
+    return HARNESS
+
+
 def binding_path() -> Path:
     import sysconfig
     return PKG / ("_qi4_torch" + sysconfig.get_config_var("EXT_SUFFIX"))

@@ -66,6 +66,10 @@ int current_device(DeviceInfo& info) {
 
 }  // namespace
 
+// One pool per device, created on first use and kept for the life of the
+// process (the pool handle belongs to the device context current then: a
+// process that calls cudaDeviceReset must not use the FP32-activation paths
+// on that device afterwards).
 cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream) {
   static std::mutex mu;
   static cudaMemPool_t pools[64] = {};

@@ -661,6 +661,11 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
     split_f32_kernel<<<blocks, 256, 0, stream>>>(static_cast<const float4*>(x), static_cast<uint2*>(scratch),
                                                   reinterpret_cast<uint2*>(static_cast<char*>(scratch) + half_bytes),
                                                   n4);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      scratch_free(scratch, stream);
+      return e;
+    }
     x_hi = scratch;
     x_lo = static_cast<char*>(scratch) + half_bytes;
   }
@@ -707,7 +712,11 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 // Device address of g_static_scratch on the current device. The name is only
 // a host-side handle; the address comes from cudaGetSymbolAddress, done once
-// per device with that device current (the first call on a device).
+// per device with that device current (the first call on a device). The
+// cached address belongs to the device context that was current then: after
+// cudaDeviceReset the module is loaded again and the array may move, so a
+// process that resets a device must not call the allocation-free entry point
+// on it again.
 cudaError_t static_scratch_address(void** out) {
   static std::mutex mu;
   static void* addr[64] = {};

@@ -1,7 +1,7 @@
 """Out-feature (column) split of W4G64 linears across GPUs, gathered over NCCL.
 
 The reference runs on one device; this is the multi-GPU layer the B200
-build adds for large prefill GEMMs. A linear's output
+build adds for large prefill GEMMs (the M = 4096 Qwen2-1.5B MLP). A linear's output
 features are split into contiguous row ranges, one per rank. In the canonical
 layout (src/qwen_int4/linear.py:39-44) row n of qweight is the K/2 bytes at
 n*K/2, its scales are row n of ``scales`` and its zero points are nibbles

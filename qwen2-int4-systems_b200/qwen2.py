@@ -7,8 +7,8 @@ The model code is the reference project's, unchanged: ``QwenInt4ForCausalLM``
 * finds the reference package (an installed ``qwen_int4``, or one installed
   with pip into ``<repo>/baseline/_ref``),
 * registers the ``b200`` backend with it (``integration.register_with_reference``),
-* builds a random-init, W4G64-RTN-quantised Qwen2-1.5B on a device - the
-  workload of BASELINE config 3 (no checkpoint or network is needed).
+* builds a random-init, W4G64-RTN-quantised Qwen2-1.5B on a device (the
+  batch-1 and batch-64 decode workloads; no checkpoint or network is needed).
 
 Quantisation follows ``quantize_symmetric_rtn`` (src/qwen_int4/quantization.py:
 87-111: per-row, per-64-group ``scale = amax / 7``, ``round(w / scale)`` clamped

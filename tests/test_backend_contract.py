@@ -105,16 +105,33 @@ def test_prims_reject_invalid_contracts_on_cpu_tensors(b200):
                                              out_features=1, in_features=96)
 
 
-def test_quantlinear_mirror_buffers_and_backend_selection(b200):
-    layer = b200.QuantLinear(1536, 256, group_size=64, bias=True)
+def _reference_or_skip(b200):
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    try:
+        return q2, q2.reference_package()
+    except ImportError:
+        pytest.skip("reference package not installed here (build() installs it into baseline/_ref)")
+
+
+def test_reference_quantlinear_selects_b200_backend(b200):
+    """The reference's own QuantLinear (src/qwen_int4/linear.py:17-72) after
+    registration: ``b200`` is an accepted backend name, unknown names are
+    still rejected, and the checkpoint buffers are the ones the kernels read."""
+    q2, ref = _reference_or_skip(b200)
+    q2.register_with_reference(ref.__name__)
+    linear = importlib.import_module(ref.__name__ + ".linear")
+    layer = linear.QuantLinear(1536, 256, group_size=64, bias=True, packing="canonical")
+    layer.set_backend("b200")
+    assert layer.backend == "b200"
+    assert "b200" in importlib.import_module(ref.__name__ + ".backends").SUPPORTED_BACKENDS
     assert layer.qweight.shape == (256 * 1536 // 2, 1) and layer.qweight.dtype == torch.uint8
     assert layer.scales.shape == (256, 24) and layer.scales.dtype == torch.float16
     assert layer.zeros.shape == ((256 * 24 + 1) // 2, 1)
-    assert layer.bias.dtype == torch.bfloat16
     with pytest.raises(ValueError):
         layer.set_backend("environment-variable-magic")
-    with pytest.raises(ValueError):
-        b200.QuantLinear(96, 4, group_size=64)
+    # On CPU tensors the b200 path fails closed (no CPU fallback).
+    with pytest.raises((ValueError, RuntimeError)):
+        layer(torch.zeros(1, 1536, dtype=torch.bfloat16))
 
 
 def _fake_reference_package(name):

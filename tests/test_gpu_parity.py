@@ -270,13 +270,21 @@ def test_pdl_on_and_off_give_identical_bits(b200, cuda_device):
     assert torch.equal(a, b)
 
 
-def test_quantlinear_mirror_dispatch(b200, cuda_device):
+def test_reference_quantlinear_dispatches_to_b200(b200, cuda_device):
+    """The reference's own QuantLinear (src/qwen_int4/linear.py:17-72) on the
+    b200 backend after ``register_with_reference``: its forward reaches the
+    CUDA kernels and matches the recorded reference output and the oracle."""
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    ref = q2.reference_package()
+    q2.register_with_reference(ref.__name__)
+    linear = importlib.import_module(ref.__name__ + ".linear")
     c = G.linear_case("lin_d3")
-    layer = b200.QuantLinear(128, 64, group_size=64, bias=True).to(cuda_device)
+    layer = linear.QuantLinear(128, 64, group_size=64, bias=True, packing="canonical").to(cuda_device)
     layer.qweight.copy_(torch.from_numpy(c["qweight"]).view_as(layer.qweight))
     layer.scales.copy_(torch.from_numpy(c["scales"]))
     layer.zeros.copy_(torch.from_numpy(c["zeros"]).view_as(layer.zeros))
     layer.bias.copy_(c["bias"])
+    layer.set_backend("b200")
     got = layer(c["x"].to(cuda_device))
     torch.testing.assert_close(got.cpu(), c["expected"], rtol=0.02, atol=0.25)
     assert_linear_close(got, _oracle_f32(c), 1e-3, "QuantLinear")
