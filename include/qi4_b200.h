@@ -158,6 +158,62 @@ QI4_API int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_
                                    const uint8_t* qweight_up, const uint16_t* scales_up_f16,
                                    const uint8_t* zeros_up, float* out, int64_t N, void* stream);
 
+/*
+ * Persistent decode chain (M <= 8 tokens): a fixed sequence of W4G64 linear
+ * stages in which stage s + 1 reads what stage s (or an earlier stage)
+ * wrote, run as ONE cooperative launch with one CTA per SM. It replaces a
+ * chain of per-linear launches at decode sizes - the reference model's
+ * QuantLinear calls of one decoder layer, src/qwen_int4/model.py:71-73
+ * (q/k/v), :122 (o_proj) and :133-135 (gate/up/down), each of which the
+ * reference dispatches separately through src/qwen_int4/linear.py:56-72 -
+ * with one weight stream that runs across stage boundaries; the math of a
+ * stage waits for its input on a device-side counter (bounded wait).
+ *
+ * A stage is 1..3 matrices sharing the activations x [M, K] (a device pointer:
+ * external input or another stage's output) with the semantics of
+ * qi4_w4g64_linear per matrix: out[m] [M, N[m]] = x @ W_m^T (+ bias[m]), FP32
+ * accumulation, cast to out_dtype. With flags = QI4_CHAIN_SWIGLU the stage
+ * holds {gate, up} (same N, no bias) and writes out[0] [M, N] in FP32 =
+ * silu(g) * u, g and u rounded to x_dtype first (the reference MLP's
+ * F.silu(gate(x).float()) * up(x).float(), model.py:133-135).
+ *
+ * qi4_chain_create validates the stages, copies every weight matrix into a
+ * prepacked tile-major layout owned by the chain (the checkpoint buffers
+ * are read, never modified; the copy is as large as qweight + scales +
+ * zeros), allocates the chain's counters and scratch with cudaMalloc, and
+ * synchronises `stream` once. The chain keeps the x / bias / out pointers:
+ * those buffers must stay allocated, and a run reads whatever x holds when
+ * it executes. qi4_chain_run enqueues one run on `stream` (no host sync);
+ * runs of one chain must not overlap on the GPU (use one stream). A wait that
+ * times out records QI4_DEVICE_WAIT_TIMEOUT for qi4_device_status.
+ * qi4_chain_info reports: [0] CTAs, [1] ring slots per CTA, [2] shared
+ * memory bytes, [3] prepacked bytes streamed per run, [4] algorithmic bytes
+ * per run (canonical formula), [5] stages. No reference counterpart.
+ */
+#define QI4_CHAIN_SWIGLU 1
+typedef struct qi4_chain_stage {
+  int32_t nmats;      /* 1..3 (2 for QI4_CHAIN_SWIGLU: gate, up) */
+  int32_t flags;      /* 0 or QI4_CHAIN_SWIGLU */
+  int64_t K;          /* shared in_features, a multiple of 64 */
+  const void* x;      /* [M, K] device pointer, 16-byte aligned */
+  int32_t x_dtype;    /* F16, BF16 or F32 */
+  int32_t bias_dtype; /* dtype of the non-null biases */
+  int32_t out_dtype;  /* F16, BF16 or F32 (ignored for SwiGLU: F32) */
+  int32_t reserved;
+  const uint8_t* qweight[3];
+  const uint16_t* scales_f16[3];
+  const uint8_t* zeros[3]; /* NULL: symmetric (all zero points 0) */
+  const void* bias[3];     /* NULL: no bias */
+  void* out[3];            /* [M, N[m]]; SwiGLU: out[0] only */
+  int64_t N[3];
+} qi4_chain_stage;
+typedef struct qi4_chain qi4_chain;
+QI4_API int qi4_chain_create(const qi4_chain_stage* stages, int n_stages, int64_t M, void* stream,
+                             qi4_chain** chain);
+QI4_API int qi4_chain_run(qi4_chain* chain, void* stream);
+QI4_API int qi4_chain_info(const qi4_chain* chain, int64_t* info);
+QI4_API int qi4_chain_destroy(qi4_chain* chain);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
  * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8, 16 or

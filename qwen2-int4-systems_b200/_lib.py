@@ -34,9 +34,28 @@ SIGNATURES = {
     "qi4_gemv_mma_plan": [_i64, _i64, _i64, _i, _i, _p],
     "qi4_device_status": [_p],
     "qi4_selftest_bounded_wait": [ctypes.c_uint64, _p],
+    "qi4_chain_create": [_p, _i, _i64, _p, ctypes.POINTER(_p)],
+    "qi4_chain_run": [_p, _p],
+    "qi4_chain_info": [_p, _p],
+    "qi4_chain_destroy": [_p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }
+
+CHAIN_SWIGLU = 1
+
+
+class ChainStage(ctypes.Structure):
+    """``qi4_chain_stage`` of include/qi4_b200.h."""
+
+    _fields_ = [
+        ("nmats", ctypes.c_int32), ("flags", ctypes.c_int32), ("K", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int32), ("bias_dtype", ctypes.c_int32),
+        ("out_dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("qweight", ctypes.c_void_p * 3), ("scales_f16", ctypes.c_void_p * 3), ("zeros", ctypes.c_void_p * 3),
+        ("bias", ctypes.c_void_p * 3), ("out", ctypes.c_void_p * 3), ("N", ctypes.c_int64 * 3),
+    ]
+
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
