@@ -176,7 +176,7 @@ __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
 // the kernel's code must stay small enough for the instruction cache, as every
 // stage walks through all of it once). Gives up, recording the error, after
 // kWaitLimitNs or once an earlier wait has timed out.
-__device__ __noinline__ void chain_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ void chain_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return;
   const uint64_t start = global_timer_ns();
 #pragma unroll 1
@@ -304,7 +304,7 @@ __device__ __forceinline__ void store_unit(int fmt, uint32_t a, uint32_t row, in
 // path through L2; not the bulk-copy unit, which streams the weights) into a
 // double-buffered raw area, the next chunk in flight while one is converted.
 // A mailbox unit whose tag is not this launch's is fetched again (bounded).
-__device__ __noinline__ void stage_activations(const ChainStage& st, int M, uint32_t xs, int xs_stride, int tid,
+__device__ __forceinline__ void stage_activations(const ChainStage& st, int M, uint32_t xs, int xs_stride, int tid,
                                                uint32_t raw, uint32_t tag16, uint32_t tag32) {
   const int fmt = st.in_fmt;
   const int E = fmt == kInTag32 ? 2 : (fmt == kInExt16 ? 8 : 4);  // elements per 16-byte unit
@@ -437,7 +437,7 @@ __device__ __forceinline__ void store_value(void* out, int dtype, int64_t i, flo
 }
 
 template <int MT, bool TWO>
-__device__ __noinline__ int compute_tiles(int t0, int t1, int aw, int bw, int G, int tile_stride, int has_zeros,
+__device__ __forceinline__ int compute_tiles(int t0, int t1, int aw, int bw, int G, int tile_stride, int has_zeros,
                                           int nslot, int pc, uint32_t ring, uint64_t* full, uint64_t* empty,
                                           uint32_t xrow, uint32_t lo_off, uint32_t red_w, int lane) {
   const int n = t1 - t0;
