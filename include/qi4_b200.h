@@ -214,6 +214,47 @@ QI4_API int qi4_chain_run(qi4_chain* chain, void* stream);
 QI4_API int qi4_chain_info(const qi4_chain* chain, int64_t* info);
 QI4_API int qi4_chain_destroy(qi4_chain* chain);
 
+/*
+ * Decode attention with in-place KV-cache append, one new token per sequence
+ * (bf16 throughout). Replaces, at decode, the reference attention's RoPE of
+ * the new query/key (src/qwen_int4/model.py:74-77), its cache growth by
+ * torch.cat and head expansion by repeat_interleave (model.py:80-91) and its
+ * masked scaled_dot_product_attention (model.py:107-118):
+ *   q', k' = RoPE(q, k) with cos/sin rows (bf16 roundings of the reference's
+ *            q*cos + rotate_half(q)*sin); no RoPE when cos = sin = NULL
+ *   k_cache[b, kvh, L_b] = k', v_cache[b, kvh, L_b] = v   (L_b = lengths[b])
+ *   out[b, h*D:(h+1)*D] = softmax(q'_h K^T * scale) V over keys 0..L_b of KV
+ *            head h / (Hq / Hkv), keys with key_mask[b, j] == 0 excluded
+ * q [B, Hq, D], k_new / v_new [B, Hkv, D] contiguous; cos / sin rows of D
+ * elements, row positions[b] (or b when positions is NULL); the caches are
+ * [B, Hkv, capacity, D] at the given batch / head strides (elements, multiples
+ * of 8; 16-byte aligned); lengths [B] int32 and the optional key_mask
+ * [B, mask_stride] uint8 are device arrays, so a captured graph advances with
+ * them. head_dim 128, at most 8 query heads per KV head. A sequence with
+ * L_b >= capacity gets a zero output and QI4_DEVICE_CACHE_FULL. lengths is
+ * not modified. No reference counterpart as a single call.
+ */
+#define QI4_DEVICE_CACHE_FULL 2
+QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const void* v_new, const void* cos,
+                                     const void* sin, const int32_t* positions, void* k_cache, void* v_cache,
+                                     int64_t cache_batch_stride, int64_t cache_head_stride, int64_t cache_capacity,
+                                     const int32_t* lengths, const uint8_t* key_mask, int64_t mask_stride,
+                                     void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
+                                     void* stream);
+
+/*
+ * Tied bf16 lm_head for decode sizes: logits[M, N] = x[M, K] @ W[N, K]^T
+ * (bf16 in, FP32 sums, bf16 out - the reference's nn.Linear lm_head over the
+ * tied embedding, src/qwen_int4/model.py:217-218,243) and/or argmax[M]
+ * (int64) = the greedy token per row, taken over the bf16 logits with the
+ * first index winning ties (generation.py:51, logits.argmax(dim=-1)).
+ * Either output may be NULL (not both): a caller that needs only the greedy
+ * token skips writing the logits. 1 <= M <= 8, K a multiple of 8 (<= 16384),
+ * weight and x 16-byte aligned. No reference counterpart as a single call.
+ */
+QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
+                                 int64_t* argmax, void* stream);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
  * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8, 16 or

@@ -17,10 +17,12 @@ from .backends import (
     set_value_checks,
     unpack_canonical_signed_int4_b200,
 )
+from .attention import b200_gqa_decode_attention
 from .integration import register_with_reference
+from .lm_head import b200_lm_head
 
 __all__ = [
-    "ALGO_AUTO", "ALGO_GEMV", "ALGO_GEMV_FMA", "ALGO_TC", "SUPPORTED_BACKENDS",
+    "ALGO_AUTO", "ALGO_GEMV", "ALGO_GEMV_FMA", "ALGO_TC", "SUPPORTED_BACKENDS", "b200_gqa_decode_attention", "b200_lm_head",
     "b200_w4g64_gate_up_silu", "b200_w4g64_linear", "b200_w4g64_linear_multi",
     "dequantize_canonical_w4g64_b200", "linear_canonical_w4g64_b200",
     "register_with_reference", "set_value_checks", "unpack_canonical_signed_int4_b200",

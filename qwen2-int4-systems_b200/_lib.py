@@ -38,6 +38,9 @@ SIGNATURES = {
     "qi4_chain_run": [_p, _p],
     "qi4_chain_info": [_p, _p],
     "qi4_chain_destroy": [_p],
+    "qi4_gqa_decode_attention": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i64,
+                                 _i64, _i64, ctypes.c_float, _p],
+    "qi4_bf16_gemv_argmax": [_p, _p, _i64, _i64, _i64, _p, _p, _p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }

@@ -1,0 +1,393 @@
+// GQA decode attention with in-place KV-cache append (sm_100a).
+//
+// Replaces, for decode steps (one new token per sequence), the reference
+// attention's cache growth and head expansion (src/qwen_int4/model.py:80-91:
+// torch.cat of the past and new key/value, repeat_interleave of the KV heads)
+// and its masked scaled_dot_product_attention (model.py:107-118), with the
+// RoPE of the new query and key (model.py:74-77) in front:
+//
+//   q', k' = RoPE(q), RoPE(k)  (bf16: q*cos and rotate_half(q)*sin each
+//                               rounded to bf16, then their sum - the
+//                               reference's three bf16 tensor ops)
+//   cache[b, kvh, L_b] = k', v       (in place; L_b = lengths[b])
+//   out[b, h] = softmax(q'_h . K[b, h / G]^T * scale + mask) V[b, h / G]
+//
+// over keys 0..L_b (the past and the new token), a key j counting only where
+// key_mask[b, j] is non-zero (left padding). FP32 scores, softmax and
+// accumulation; output bf16.
+//
+// Work split ("flash decoding"): a CTA owns one (batch, KV head, 64-key
+// split) and all G query heads of that KV head, so K and V are read once for
+// the group (no expansion). 4 warps take 16 keys each, 8 at a time: lane
+// (key kk = lane / 4, quarter dq = lane % 4) dots its 32 dims of the key with
+// the G queries (held in shared memory, FP32), a 2-step shuffle sums the
+// quarters; per head an online softmax (running max, rescaled sums) and
+// P.V with lane = 4 output dims. The CTA's partial (max, sum, 128 sums per
+// head) goes to scratch; a second kernel combines the splits per head.
+#include <algorithm>
+#include <cmath>
+
+#include "qi4_common.cuh"
+
+namespace qi4 {
+
+__device__ int g_attention_error;
+
+namespace {
+
+constexpr int kD = 128;          // head dim
+constexpr int kMaxGroup = 8;     // query heads per KV head
+constexpr int kSplitKeys = 64;   // keys per CTA
+constexpr int kWarps = 4;
+constexpr int kQPad = 36;        // floats per (head, quarter) row: 32 + 4 (bank spread)
+
+struct AttnArgs {
+  const __nv_bfloat16* q;      // [B, Hq, D]
+  const __nv_bfloat16* k_new;  // [B, Hkv, D]
+  const __nv_bfloat16* v_new;  // [B, Hkv, D]
+  const __nv_bfloat16* cos;    // rows of D (row positions[b], or b), or null: no RoPE
+  const __nv_bfloat16* sin;
+  const int32_t* positions;    // [B] row of cos/sin per sequence, or null: row b
+  __nv_bfloat16* k_cache;      // [B][Hkv][cap][D] at the given strides (elements)
+  __nv_bfloat16* v_cache;
+  int64_t cb, ch;              // batch / head strides of the caches
+  const int32_t* lengths;      // [B] past length L_b (the new token goes at L_b)
+  const uint8_t* key_mask;     // [B, mask_stride], or null
+  int64_t mask_stride;
+  float* partial;              // [B][Hkv][splits][G][kD + 2]
+  int B, Hq, Hkv, G, cap, splits;
+  float scale;
+};
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// RoPE of element d of a head vector x (bf16 roundings as the reference's
+// tensor ops: x*cos, rotate_half(x)*sin, their sum).
+__device__ __forceinline__ float rope(const __nv_bfloat16* x, const __nv_bfloat16* c, const __nv_bfloat16* s, int d) {
+  const float xd = bf(x[d]);
+  const float rh = d < kD / 2 ? -bf(x[d + kD / 2]) : bf(x[d - kD / 2]);
+  return rbf(rbf(xd * bf(c[d])) + rbf(rh * bf(s[d])));
+}
+
+__global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs a) {
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int L = a.lengths[b];  // past keys; the new one is key L
+  const int nkeys = L + 1;
+  const int k0 = split * kSplitKeys;
+  if (k0 >= nkeys || L >= a.cap) return;  // nothing of this sequence here (or no room: host-checked)
+  const int k1 = min(nkeys, k0 + kSplitKeys);
+  const int G = a.G;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  __shared__ __align__(16) float q_s[kMaxGroup][4][kQPad];  // RoPE'd queries, FP32, by head and quarter
+  __shared__ float p_s[kWarps][8][kMaxGroup];          // softmax weights of a warp's 8 keys
+  __shared__ float knew_s[kD], vnew_s[kD];             // the new key (RoPE'd) and value
+  __shared__ float red_m[kWarps][kMaxGroup], red_l[kWarps][kMaxGroup];
+  __shared__ float red_acc[kWarps][kMaxGroup][kD];
+
+  const __nv_bfloat16* cs = nullptr;
+  const __nv_bfloat16* sn = nullptr;
+  if (a.cos) {
+    const int64_t row = a.positions ? a.positions[b] : b;
+    cs = a.cos + row * kD;
+    sn = a.sin + row * kD;
+  }
+  for (int i = tid; i < G * kD; i += blockDim.x) {
+    const int h = i / kD, d = i - h * kD;
+    const __nv_bfloat16* qh = a.q + ((int64_t)b * a.Hq + kvh * G + h) * kD;
+    const float v = cs ? rope(qh, cs, sn, d) : bf(qh[d]);
+    q_s[h][d >> 5][d & 31] = v;
+  }
+  const bool has_new = k0 <= L && L < k1;
+  if (has_new) {
+    // The new key / value: used from here, and appended to the cache.
+    const __nv_bfloat16* kn = a.k_new + ((int64_t)b * a.Hkv + kvh) * kD;
+    const __nv_bfloat16* vn = a.v_new + ((int64_t)b * a.Hkv + kvh) * kD;
+    __nv_bfloat16* kc = a.k_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
+    __nv_bfloat16* vc = a.v_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
+    for (int d = tid; d < kD; d += blockDim.x) {
+      const float kv = cs ? rope(kn, cs, sn, d) : bf(kn[d]);
+      knew_s[d] = kv;
+      vnew_s[d] = bf(vn[d]);
+      kc[d] = __float2bfloat16_rn(kv);  // exact: kv is a bf16 value
+      vc[d] = vn[d];
+    }
+  }
+  __syncthreads();
+
+  const int kk = lane >> 2, dq = lane & 3;
+  float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][4];
+#pragma unroll
+  for (int h = 0; h < kMaxGroup; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
+  }
+  const __nv_bfloat16* kbase = a.k_cache + b * a.cb + kvh * a.ch;
+  const __nv_bfloat16* vbase = a.v_cache + b * a.cb + kvh * a.ch;
+  const uint8_t* mrow = a.key_mask ? a.key_mask + (int64_t)b * a.mask_stride : nullptr;
+
+  for (int g0 = k0 + warp * 8; g0 < k1; g0 += kWarps * 8) {
+    // Scores of this lane's key (kk) over its 32 dims for every head.
+    const int key = g0 + kk;
+    const bool valid = key < k1 && (!mrow || mrow[key] != 0);
+    float s[kMaxGroup];
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) s[h] = 0.f;
+    if (key < k1) {
+      float kf[32];
+      if (key == L && has_new) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) kf[j] = knew_s[dq * 32 + j];
+      } else {
+        const uint4* kp = reinterpret_cast<const uint4*>(kbase + (int64_t)key * kD + dq * 32);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 w = kp[c];
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kf[c * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
+            kf[c * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) {
+        if (h < G) {
+          const float4* qh = reinterpret_cast<const float4*>(&q_s[h][dq][0]);
+          float t = 0.f;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 qv = qh[c];
+            t = fmaf(qv.x, kf[4 * c], t);
+            t = fmaf(qv.y, kf[4 * c + 1], t);
+            t = fmaf(qv.z, kf[4 * c + 2], t);
+            t = fmaf(qv.w, kf[4 * c + 3], t);
+          }
+          s[h] = t;
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) {
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+      s[h] = valid ? s[h] * a.scale : -INFINITY;
+    }
+    // Online softmax over this group of 8 keys, per head.
+#pragma unroll
+    for (int h = 0; h < kMaxGroup; ++h) {
+      if (h >= G) continue;
+      float mx = s[h];
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(m[h], mx);
+      const float alpha = mn == -INFINITY ? 1.f : __expf(m[h] - mn);
+      const float p = s[h] == -INFINITY ? 0.f : __expf(s[h] - mn);
+      m[h] = mn;
+      l[h] = l[h] * alpha + p;  // per key kk (replicated over dq); summed over kk at the end
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[h][j] *= alpha;
+      if (dq == 0) p_s[warp][kk][h] = p;
+    }
+    __syncwarp();
+    // P.V: lane owns output dims 4 lane .. 4 lane + 3.
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int key2 = g0 + e;
+      if (key2 >= k1) break;
+      float vf[4];
+      if (key2 == L && has_new) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) vf[j] = vnew_s[lane * 4 + j];
+      } else {
+        const uint2 w = *reinterpret_cast<const uint2*>(vbase + (int64_t)key2 * kD + lane * 4);
+        vf[0] = __uint_as_float(w.x << 16);
+        vf[1] = __uint_as_float(w.x & 0xFFFF0000u);
+        vf[2] = __uint_as_float(w.y << 16);
+        vf[3] = __uint_as_float(w.y & 0xFFFF0000u);
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxGroup; ++h) {
+        if (h >= G) continue;
+        const float p = p_s[warp][e][h];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[h][j] = fmaf(p, vf[j], acc[h][j]);
+      }
+    }
+    __syncwarp();
+  }
+  // Per warp: sum l over the 8 key lanes (each value is replicated 4 times).
+#pragma unroll
+  for (int h = 0; h < kMaxGroup; ++h) {
+    if (h >= G) continue;
+    float t = l[h];
+    t += __shfl_xor_sync(0xffffffffu, t, 4);
+    t += __shfl_xor_sync(0xffffffffu, t, 8);
+    t += __shfl_xor_sync(0xffffffffu, t, 16);
+    if (lane == 0) {
+      red_m[warp][h] = m[h];
+      red_l[warp][h] = t;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) red_acc[warp][h][lane * 4 + j] = acc[h][j];
+  }
+  __syncthreads();
+  // Combine the warps into the CTA's partial (warps without keys have m = -inf).
+  float* out = a.partial + (((int64_t)b * a.Hkv + kvh) * a.splits + split) * G * (kD + 2);
+  for (int i = tid; i < G * kD; i += blockDim.x) {
+    const int h = i / kD, d = i - h * kD;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, red_m[w][h]);
+    float ls = 0.f, as = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = red_m[w][h] == -INFINITY ? 0.f : __expf(red_m[w][h] - mm);
+      ls += red_l[w][h] * f;
+      as += red_acc[w][h][d] * f;
+    }
+    float* o = out + h * (kD + 2);
+    o[2 + d] = as;
+    if (d == 0) {
+      o[0] = mm;
+      o[1] = ls;
+    }
+  }
+}
+
+// out[b, h * D + d] = sum_s e^(m_s - M) acc_s[d] / sum_s e^(m_s - M) l_s.
+// A sequence whose cache is full (L_b >= cap) was not processed: its output
+// is zero (and qi4_device_status reports QI4_DEVICE_CACHE_FULL).
+__global__ void gqa_combine_kernel(const float* __restrict__ partial, const int32_t* __restrict__ lengths,
+                                   __nv_bfloat16* __restrict__ out, int Hkv, int G, int splits, int cap) {
+  const int h = blockIdx.x, b = blockIdx.y;  // query head
+  const int kvh = h / G, hg = h - kvh * G;
+  const int L = lengths[b];
+  if (L >= cap) {
+    for (int d = threadIdx.x; d < kD; d += blockDim.x) out[((int64_t)b * Hkv * G + h) * kD + d] = __float2bfloat16_rn(0.f);
+    if (threadIdx.x == 0 && h == 0) atomicOr(&g_attention_error, 2);
+    return;
+  }
+  const int used = min(splits, (L + 1 + kSplitKeys - 1) / kSplitKeys);
+  const float* base = partial + ((int64_t)b * Hkv + kvh) * splits * G * (kD + 2) + hg * (kD + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < used; ++s) M = fmaxf(M, base[(int64_t)s * G * (kD + 2)]);
+  for (int d = threadIdx.x; d < kD; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < used; ++s) {
+      const float* p = base + (int64_t)s * G * (kD + 2);
+      const float f = p[0] == -INFINITY ? 0.f : __expf(p[0] - M);
+      num += p[2 + d] * f;
+      den += p[1] * f;
+    }
+    out[((int64_t)b * Hkv * G + h) * kD + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+  }
+}
+
+}  // namespace
+
+int attention_splits(int cap) { return (cap + kSplitKeys - 1) / kSplitKeys; }
+
+cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_new, const void* cos, const void* sin,
+                              const int32_t* positions, void* k_cache, void* v_cache, int64_t cb, int64_t ch,
+                              const int32_t* lengths, const uint8_t* key_mask, int64_t mask_stride, void* out,
+                              float* partial, int B, int Hq, int Hkv, int cap, float scale, cudaStream_t stream) {
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k_new = static_cast<const __nv_bfloat16*>(k_new);
+  a.v_new = static_cast<const __nv_bfloat16*>(v_new);
+  a.cos = static_cast<const __nv_bfloat16*>(cos);
+  a.sin = static_cast<const __nv_bfloat16*>(sin);
+  a.positions = positions;
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.cb = cb;
+  a.ch = ch;
+  a.lengths = lengths;
+  a.key_mask = key_mask;
+  a.mask_stride = mask_stride;
+  a.partial = partial;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.cap = cap;
+  a.splits = attention_splits(cap);
+  a.scale = scale;
+  gqa_decode_kernel<<<dim3(a.splits, Hkv, B), kWarps * 32, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  gqa_combine_kernel<<<dim3(Hq, B), kD, 0, stream>>>(partial, lengths, static_cast<__nv_bfloat16*>(out), Hkv, a.G,
+                                                     a.splits, cap);
+  return cudaGetLastError();
+}
+
+int read_attention_error(cudaStream_t stream) {
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_attention_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return -1;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return -1;
+  if (v) {
+    const int zero = 0;
+    cudaMemcpyToSymbolAsync(g_attention_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
+  }
+  return v;
+}
+
+}  // namespace qi4
+
+extern "C" QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const void* v_new, const void* cos,
+                                                const void* sin, const int32_t* positions, void* k_cache,
+                                                void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                                                int64_t cache_capacity, const int32_t* lengths,
+                                                const uint8_t* key_mask, int64_t mask_stride, void* out, int64_t B,
+                                                int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
+                                                void* stream_ptr) {
+  using namespace qi4;
+  clear_error();
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !lengths || !out || (!cos != !sin)) {
+    set_error("q, k_new, v_new, the caches, lengths and out must be non-null (cos and sin both or neither)");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || cache_capacity <= 0 || B > 65535 || Hkv > 65535) {
+    set_error("B, Hq, Hkv and the cache capacity must be positive");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (head_dim != kD || Hq % Hkv || Hq / Hkv > kMaxGroup) {
+    set_error("decode attention supports head_dim 128 and up to %d query heads per KV head (got %lld, %lld/%lld)",
+              kMaxGroup, (long long)head_dim, (long long)Hq, (long long)Hkv);
+    return QI4_ERR_SHAPE;
+  }
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(k_cache) || !al16(v_cache) || cache_batch_stride % 8 || cache_head_stride % 8 || !al16(q) ||
+      !al16(k_new) || !al16(v_new)) {
+    set_error("caches and q/k/v must be 16-byte aligned with strides a multiple of 8 elements");
+    return QI4_ERR_ALIGNMENT;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int splits = attention_splits((int)std::min<int64_t>(cache_capacity, 1 << 24));
+  void* partial = nullptr;
+  const size_t bytes = (size_t)B * Hkv * splits * (Hq / Hkv) * (kD + 2) * sizeof(float);
+  if (scratch_alloc(&partial, bytes, stream) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cannot allocate %zu bytes of attention scratch", bytes);
+    return QI4_ERR_LAUNCH;
+  }
+  const cudaError_t e = launch_gqa_decode(q, k_new, v_new, cos, sin, positions, k_cache, v_cache, cache_batch_stride,
+                                          cache_head_stride, lengths, key_mask, mask_stride, out,
+                                          static_cast<float*>(partial), (int)B, (int)Hq, (int)Hkv,
+                                          (int)cache_capacity, scale, stream);
+  scratch_free(partial, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("decode attention launch failed: %s", cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
+  return QI4_OK;
+}

@@ -15,7 +15,8 @@
 #include "qi4_common.cuh"
 
 namespace qi4 {
-int read_chain_error(cudaStream_t stream);  // decode_chain.cu
+int read_chain_error(cudaStream_t stream);      // decode_chain.cu
+int read_attention_error(cudaStream_t stream);  // attention.cu
 }
 
 namespace qi4 {
@@ -494,7 +495,8 @@ int qi4_device_status(void* stream) {
   const int v1 = read_gemv_mma_error(static_cast<cudaStream_t>(stream));
   const int v2 = read_gemm_tc_error(static_cast<cudaStream_t>(stream));
   const int v3 = read_chain_error(static_cast<cudaStream_t>(stream));
-  const int v = (v1 < 0 || v2 < 0 || v3 < 0) ? -1 : (v1 | v2 | v3);
+  const int v4 = read_attention_error(static_cast<cudaStream_t>(stream));
+  const int v = (v1 < 0 || v2 < 0 || v3 < 0 || v4 < 0) ? -1 : (v1 | v2 | v3 | v4);
   if (v < 0) {
     set_error("cannot read the device error flags: %s", cudaGetErrorString(cudaGetLastError()));
     return QI4_ERR_LAUNCH;

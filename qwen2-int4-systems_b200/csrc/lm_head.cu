@@ -1,0 +1,222 @@
+// Tied bf16 lm_head: logits = x @ W^T as a streaming GEMV, with the greedy
+// token (argmax) fused in. sm_100a.
+//
+// Replaces, for decode sizes (M <= 8 tokens), the reference's lm_head
+// (src/qwen_int4/model.py:217-218,243: nn.Linear over the tied embedding,
+// bf16 weight [V, D]) and the greedy pick on its output
+// (src/qwen_int4/generation.py:51: logits[:, -1].argmax(dim=-1)).
+// The weight (467 MB for Qwen2-1.5B) is read once per call with 16-byte
+// streaming loads; each warp walks its rows two at a time (all twelve loads of
+// a lane in flight), dots them with the tokens' activations (bf16 in shared
+// memory, FP32 products and sums), sums the lanes with shuffles and rounds the
+// logit to bf16 - the value the reference's bf16 linear returns. The argmax
+// is over those rounded values, first index on ties (torch.argmax's rule):
+// each CTA keeps its best (value, row) per token and merges it into a 64-bit
+// key (order-preserving bits of the value, inverted row) with one atomicMax;
+// a final kernel turns the keys into indices. Writing the full logits is
+// optional (a caller that only needs the greedy token skips the 0.3 MB/token
+// store).
+#include "qi4_common.cuh"
+
+namespace qi4 {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxTok = 8;
+constexpr int kRows = 2;  // rows per warp iteration
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) { return ldg_stream16(p); }
+
+// Order-preserving unsigned image of a float (-0 taken as +0).
+__device__ __forceinline__ uint32_t ordered(float v) {
+  uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads) gemv_argmax_kernel(const __nv_bfloat16* __restrict__ W,
+                                                               const __nv_bfloat16* __restrict__ x, int64_t N,
+                                                               int K, __nv_bfloat16* __restrict__ logits,
+                                                               unsigned long long* __restrict__ keys,
+                                                               int64_t rows_per_cta) {
+  extern __shared__ uint4 xs_raw[];  // [M][K] bf16
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < M * K / 8; i += kThreads) xs_raw[i] = reinterpret_cast<const uint4*>(x)[i];
+  __syncthreads();
+  const uint32_t xs = (uint32_t)__cvta_generic_to_shared(xs_raw);
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta, r1 = min(N, r0 + rows_per_cta);
+  const int chunks = K / 8;  // 16-byte chunks per row
+  float best[M];
+  int64_t best_row[M];
+#pragma unroll
+  for (int t = 0; t < M; ++t) {
+    best[t] = -INFINITY;
+    best_row[t] = -1;
+  }
+  for (int64_t r = r0 + warp * kRows; r < r1; r += (kThreads / 32) * kRows) {
+    float acc[kRows][M];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j)
+#pragma unroll
+      for (int t = 0; t < M; ++t) acc[j][t] = 0.f;
+    for (int c0 = lane; c0 < chunks; c0 += 32 * 6) {
+      uint4 w[kRows][6];
+#pragma unroll
+      for (int j = 0; j < kRows; ++j)
+#pragma unroll
+        for (int u = 0; u < 6; ++u) {
+          const int c = c0 + u * 32;
+          w[j][u] = (r + j < r1 && c < chunks) ? ld_stream(W + (r + j) * K + (int64_t)c * 8) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+      for (int u = 0; u < 6; ++u) {
+        const int c = c0 + u * 32;
+        if (c >= chunks) break;
+#pragma unroll
+        for (int t = 0; t < M; ++t) {
+          uint4 xv;
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(xv.x), "=r"(xv.y), "=r"(xv.z), "=r"(xv.w)
+                       : "r"(xs + (uint32_t)((t * K + c * 8) * 2)));
+          const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+          for (int j = 0; j < kRows; ++j) {
+            const uint32_t ww[4] = {w[j][u].x, w[j][u].y, w[j][u].z, w[j][u].w};
+            float a = acc[j][t];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              a = fmaf(__uint_as_float(ww[e] << 16), __uint_as_float(xw[e] << 16), a);
+              a = fmaf(__uint_as_float(ww[e] & 0xFFFF0000u), __uint_as_float(xw[e] & 0xFFFF0000u), a);
+            }
+            acc[j][t] = a;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+      if (r + j >= r1) break;
+#pragma unroll
+      for (int t = 0; t < M; ++t) {
+        float v = acc[j][t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const __nv_bfloat16 rb = __float2bfloat16_rn(v);
+        const float vr = __bfloat162float(rb);
+        if (lane == 0 && logits) logits[(int64_t)t * N + r + j] = rb;
+        if (vr > best[t]) {  // rows ascend, so a later row never wins a tie
+          best[t] = vr;
+          best_row[t] = r + j;
+        }
+      }
+    }
+  }
+  // CTA merge (warps in order, ties to the smaller row), then one atomic per token.
+  __shared__ float wb[kThreads / 32][kMaxTok];
+  __shared__ long long wr[kThreads / 32][kMaxTok];
+  if (lane == 0) {
+#pragma unroll
+    for (int t = 0; t < M; ++t) {
+      wb[warp][t] = best[t];
+      wr[warp][t] = best_row[t];
+    }
+  }
+  __syncthreads();
+  if (tid < M) {
+    float bv = -INFINITY;
+    long long br = -1;
+    for (int w = 0; w < kThreads / 32; ++w) {
+      if (wr[w][tid] < 0) continue;
+      if (br < 0 || wb[w][tid] > bv || (wb[w][tid] == bv && wr[w][tid] < br)) {
+        bv = wb[w][tid];
+        br = wr[w][tid];
+      }
+    }
+    if (br >= 0) {
+      const unsigned long long key = ((unsigned long long)ordered(bv) << 32) | (0xFFFFFFFFull - (unsigned long long)br);
+      atomicMax(keys + tid, key);
+    }
+  }
+}
+
+__global__ void argmax_finalize_kernel(const unsigned long long* keys, int64_t* out, int M) {
+  const int t = threadIdx.x;
+  if (t < M) out[t] = keys[t] ? (int64_t)(0xFFFFFFFFull - (keys[t] & 0xFFFFFFFFull)) : 0;
+}
+
+template <int M>
+cudaError_t launch_m(const void* w, const void* x, int64_t N, int K, void* logits, unsigned long long* keys,
+                     int grid, int64_t rows_per_cta, cudaStream_t stream) {
+  const size_t smem = (size_t)M * K * 2;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(gemv_argmax_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  gemv_argmax_kernel<M><<<grid, kThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(w),
+                                                          static_cast<const __nv_bfloat16*>(x), N, K,
+                                                          static_cast<__nv_bfloat16*>(logits), keys, rows_per_cta);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+}  // namespace qi4
+
+extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N,
+                                            void* logits, int64_t* argmax, void* stream_ptr) {
+  using namespace qi4;
+  clear_error();
+  if (!weight || !x || (!logits && !argmax)) {
+    set_error("weight and x must be non-null, and at least one of logits / argmax");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (M < 1 || M > kMaxTok || K <= 0 || K % 8 || K > 16384 || N <= 0 || N >= (int64_t)1 << 32) {
+    set_error("lm_head GEMV takes 1 <= M <= %d, K a multiple of 8 up to 16384 and N < 2^32 (got M=%lld K=%lld "
+              "N=%lld)", kMaxTok, (long long)M, (long long)K, (long long)N);
+    return QI4_ERR_SHAPE;
+  }
+  if ((reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(x)) & 15) {
+    set_error("weight and x must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  void* keys = nullptr;
+  if (argmax) {
+    if (scratch_alloc(&keys, kMaxTok * sizeof(unsigned long long), stream) != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cannot allocate the argmax scratch");
+      return QI4_ERR_LAUNCH;
+    }
+    cudaMemsetAsync(keys, 0, kMaxTok * sizeof(unsigned long long), stream);
+  }
+  const int grid = sms * 4;
+  const int64_t rows_per_cta = ((N + grid - 1) / grid + kRows - 1) / kRows * kRows;
+  auto k = static_cast<unsigned long long*>(keys);
+  cudaError_t e;
+  switch (M) {
+    case 1: e = launch_m<1>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 2: e = launch_m<2>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 3: e = launch_m<3>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 4: e = launch_m<4>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 5: e = launch_m<5>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 6: e = launch_m<6>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    case 7: e = launch_m<7>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
+    default: e = launch_m<8>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;  // M == 8
+  }
+  if (e == cudaSuccess && argmax) {
+    argmax_finalize_kernel<<<1, 32, 0, stream>>>(k, argmax, (int)M);
+    e = cudaGetLastError();
+  }
+  if (keys) scratch_free(keys, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("lm_head GEMV launch failed: %s", cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
+  return QI4_OK;
+}

@@ -14,6 +14,10 @@ commit instead is a three-line change to those tables.
 the ``b200`` backend: one launch computes ``silu(gate(x)) * up(x)`` (each
 projection rounded to ``x.dtype`` first, as QuantLinear returns it) in FP32,
 which ``down_proj`` consumes exactly as the reference MLP passes it.
+
+``fast_attention=True`` routes the reference attention's decode steps through
+the b200 decode attention (RoPE + in-place KV append + GQA attention in one
+call; see the ``attention`` module), keeping the reference's cache tuples.
 """
 
 from __future__ import annotations
@@ -26,14 +30,21 @@ from .backends import b200_w4g64_gate_up_silu, b200_w4g64_linear
 BACKEND = "b200"
 
 
-def register_with_reference(package: str = "qwen_int4", *, fuse_mlp: bool = False) -> None:
+def register_with_reference(package: str = "qwen_int4", *, fuse_mlp: bool = False,
+                            fast_attention: bool = False) -> None:
     """Make ``backend="b200"`` valid in the reference's QuantLinear. Idempotent.
 
     ``fuse_mlp`` selects whether the reference MLP uses the fused gate/up
-    SwiGLU call on that backend; each call sets it (default off).
+    SwiGLU call on that backend; ``fast_attention`` whether the reference
+    attention's decode steps use the b200 decode attention with in-place KV
+    cache append (attention.patch_reference_attention). Each call sets both
+    switches (default off).
     """
     _register_linear(package)
     _set_mlp_fusion(package, fuse_mlp)
+    from .attention import patch_reference_attention
+
+    patch_reference_attention(package, fast_attention)
 
 
 def _register_linear(package: str) -> None:

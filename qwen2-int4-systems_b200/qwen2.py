@@ -91,15 +91,15 @@ def quantize_asymmetric_rtn_torch(weight: torch.Tensor, group_size: int = 64):
 
 @torch.no_grad()
 def build_random_qwen2(config=None, *, device="cuda", seed: int = 0, backend: str = "b200",
-                       fuse_mlp: bool = False):
+                       fuse_mlp: bool = False, fast_attention: bool = False):
     """Reference ``QwenInt4ForCausalLM`` with random W4G64 RTN weights on ``device``.
 
     Every QuantLinear gets ``quantize_symmetric_rtn(bf16(randn * 0.02))``,
     q/k/v biases ~N(0, 0.02), embeddings ~N(0, 0.02) (tied lm_head), norms 1.
-    ``fuse_mlp`` is passed to ``register_with_reference``.
+    ``fuse_mlp`` and ``fast_attention`` are passed to ``register_with_reference``.
     """
     ref = reference_package()
-    register_with_reference(ref.__name__, fuse_mlp=fuse_mlp)
+    register_with_reference(ref.__name__, fuse_mlp=fuse_mlp, fast_attention=fast_attention)
     from qwen_int4.linear import QuantLinear
     from qwen_int4.model import QwenInt4ForCausalLM
     from qwen_int4.quantization import PackingFormat

@@ -1,0 +1,142 @@
+"""Decode attention with in-place KV append (qi4_gqa_decode_attention) on a GPU.
+
+Against the reference attention's own math on the same inputs (RoPE as three
+bf16 tensor ops, model.py:74-77; repeat_interleave of the KV heads and a
+masked softmax in FP32, model.py:90-118): outputs within 1.5e-2 absolute /
+cosine >= 0.99999 (the bf16 output's own rounding is ~4e-3 relative), the
+appended cache entries bit-exact. Then the reference model itself on the
+b200 backend with ``fast_attention=True``: cached decode agrees with the full
+forward and with the unpatched decode, and a forked cache keeps both
+continuations apart.
+"""
+
+import importlib
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rotate_half(x):
+    a, b = x.chunk(2, dim=-1)
+    return torch.cat((-b, a), dim=-1)
+
+
+def _reference(q, k_new, v_new, cos, sin, past_k, past_v, mask, G):
+    """The reference model's decode attention (model.py:74-118), FP32 softmax."""
+    q = q.unsqueeze(2)  # [B, Hq, 1, D]
+    k = k_new.unsqueeze(2)
+    c, s = cos[:, None, None, :], sin[:, None, None, :]
+    q = q * c + _rotate_half(q) * s
+    k = k * c + _rotate_half(k) * s
+    K = torch.cat((past_k, k), dim=2).repeat_interleave(G, dim=1).float()
+    V = torch.cat((past_v, v_new.unsqueeze(2)), dim=2).repeat_interleave(G, dim=1).float()
+    scores = (q.float() @ K.transpose(-1, -2)) * q.shape[-1] ** -0.5
+    if mask is not None:
+        scores = scores.masked_fill(~mask.bool()[:, None, None, :], float("-inf"))
+    out = torch.softmax(scores, dim=-1) @ V
+    return out.squeeze(2).reshape(q.shape[0], -1).to(torch.bfloat16), k.squeeze(2)
+
+
+@pytest.mark.parametrize("B,L,Hq,Hkv", [(1, 0, 12, 2), (1, 5, 12, 2), (3, 63, 12, 2), (2, 64, 12, 2),
+                                        (2, 130, 8, 8), (4, 700, 12, 2), (64, 333, 12, 2)])
+def test_decode_attention_matches_reference_math(b200, cuda_device, B, L, Hq, Hkv):
+    g = torch.Generator(device="cpu").manual_seed(L * 7 + B)
+    D, cap = 128, L + 1 + 37
+    bf = dict(dtype=torch.bfloat16, device=cuda_device)
+    q = torch.randn(B, Hq, D, generator=g).to(**bf)
+    k_new = torch.randn(B, Hkv, D, generator=g).to(**bf)
+    v_new = torch.randn(B, Hkv, D, generator=g).to(**bf)
+    pos = torch.arange(B) + L
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float32) / D))
+    f = pos[:, None].float() * inv[None, :]
+    emb = torch.cat((f, f), dim=-1)
+    cos, sin = emb.cos().to(**bf), emb.sin().to(**bf)
+    kc = torch.randn(B, Hkv, cap, D, generator=g).to(**bf)
+    vc = torch.randn(B, Hkv, cap, D, generator=g).to(**bf)
+    past_k, past_v = kc[:, :, :L].clone(), vc[:, :, :L].clone()
+    mask = torch.ones(B, L + 1, dtype=torch.bool)
+    for b in range(B):  # left padding: the first (b * 3) % (L + 1) keys invalid
+        mask[b, : (b * 3) % (L + 1)] = False
+    mask = mask.to(cuda_device)
+    lengths = torch.full((B,), L, dtype=torch.int32, device=cuda_device)
+    out = b200.b200_gqa_decode_attention(q, k_new, v_new, kc, vc, lengths, cos=cos, sin=sin, key_mask=mask)
+    torch.cuda.synchronize()
+    ref, k_roped = _reference(q, k_new, v_new, cos, sin, past_k, past_v, mask, Hq // Hkv)
+    cosine = torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), dim=0)
+    assert float((out.float() - ref.float()).abs().max()) <= 1.5e-2
+    assert float(cosine) >= 0.99999
+    assert torch.equal(kc[:, :, L], k_roped) and torch.equal(vc[:, :, L], v_new)  # appended in place
+    assert torch.equal(kc[:, :, :L], past_k) and torch.equal(vc[:, :, :L], past_v)  # past untouched
+
+
+def test_full_cache_gives_zero_output_and_a_status(b200, cuda_device):
+    lib = importlib.import_module(b200.__name__ + "._lib").load()
+    bf = dict(dtype=torch.bfloat16, device=cuda_device)
+    q, kv = torch.randn(1, 12, 128).to(**bf), torch.randn(1, 2, 128).to(**bf)
+    kc, vc = torch.zeros(1, 2, 8, 128, **bf), torch.zeros(1, 2, 8, 128, **bf)
+    lengths = torch.tensor([8], dtype=torch.int32, device=cuda_device)  # no room for key 8
+    out = b200.b200_gqa_decode_attention(q, kv, kv, kc, vc, lengths)
+    assert torch.count_nonzero(out) == 0
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 2
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def _cos(a, b):
+    return float(torch.nn.functional.cosine_similarity(a.float().flatten(), b.float().flatten(), dim=0))
+
+
+def test_reference_model_decode_with_fast_attention(b200, cuda_device):
+    """The reference model (2 layers) on b200 with the decode attention
+    patched in: each cached step agrees with the full forward, and with the
+    same steps through the reference's own attention code."""
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    cfg = q2.qwen2_config(num_hidden_layers=2, vocab_size=512)
+    model = q2.build_random_qwen2(cfg, device=cuda_device, seed=3, fast_attention=True)
+    ref_name = q2.reference_package().__name__
+    tokens = torch.randint(0, 512, (2, 12), generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    mask = torch.ones(2, 12, dtype=torch.bool, device=cuda_device)
+    mask[1, :3] = False  # left padding of the second sequence
+    try:
+        with torch.inference_mode():
+            full = model(tokens, attention_mask=mask)
+            fast_steps = []
+            _, cache = model(tokens[:, :6], attention_mask=mask[:, :6], use_cache=True)
+            for t in range(6, 12):
+                logits, cache = model(tokens[:, t:t + 1], attention_mask=mask[:, :t + 1], past_key_values=cache,
+                                      use_cache=True)
+                fast_steps.append(logits[:, -1])
+            assert cache[0][0].shape[2] == 12
+            q2.register_with_reference(ref_name, fast_attention=False)
+            _, cache = model(tokens[:, :6], attention_mask=mask[:, :6], use_cache=True)
+            for i, t in enumerate(range(6, 12)):
+                logits, cache = model(tokens[:, t:t + 1], attention_mask=mask[:, :t + 1], past_key_values=cache,
+                                      use_cache=True)
+                assert _cos(fast_steps[i], logits[:, -1]) > 0.9999
+                assert _cos(fast_steps[i], full[:, t]) > 0.9999
+    finally:
+        q2.register_with_reference(ref_name, fast_attention=False)
+
+
+def test_forked_cache_continuations_stay_apart(b200, cuda_device):
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    cfg = q2.qwen2_config(num_hidden_layers=2, vocab_size=512)
+    model = q2.build_random_qwen2(cfg, device=cuda_device, seed=4, fast_attention=True)
+    ref_name = q2.reference_package().__name__
+    prompt = torch.randint(0, 512, (1, 7), generator=torch.Generator().manual_seed(2)).to(cuda_device)
+    a, b = torch.tensor([[5]], device=cuda_device), torch.tensor([[9]], device=cuda_device)
+    try:
+        with torch.inference_mode():
+            _, cache = model(prompt, use_cache=True)
+            _, cache = model(a, past_key_values=cache, use_cache=True)  # capacity buffers from here on
+            la, ca = model(a, past_key_values=cache, use_cache=True)
+            lb, cb = model(b, past_key_values=cache, use_cache=True)  # same prefix: must copy, not overwrite
+            la2, _ = model(b, past_key_values=ca, use_cache=True)
+            full_a = model(torch.cat((prompt, a, a, b), dim=1))
+            full_b = model(torch.cat((prompt, a, b), dim=1))
+        assert _cos(la2[:, -1], full_a[:, -1]) > 0.9999
+        assert _cos(lb[:, -1], full_b[:, -1]) > 0.9999
+        assert not torch.equal(ca[0][0], cb[0][0])
+    finally:
+        q2.register_with_reference(ref_name, fast_attention=False)
