@@ -252,6 +252,15 @@ QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const voi
  * token skips writing the logits. 1 <= M <= 8, K a multiple of 8 (<= 16384),
  * weight and x 16-byte aligned. No reference counterpart as a single call.
  */
+/* Residual add + RMSNorm at a decoder block boundary (the reference's
+ * DecoderLayer / RMSNorm, src/qwen_int4/model.py:31-42,151-159), in place on
+ * the bf16 residual stream h [B, D]:
+ *   h   = bf16(h + bf16(delta))   (delta [B, D] of BF16 or F32; NULL: none)
+ *   out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * weight)   (FP32 statistics)
+ * D <= 4096. No reference counterpart as a single call. */
+QI4_API int qi4_add_rmsnorm(void* h, const void* delta, int delta_dtype, const void* weight, void* out, int64_t B,
+                            int64_t D, float eps, void* stream);
+
 QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
                                  int64_t* argmax, void* stream);
 

@@ -41,6 +41,7 @@ SIGNATURES = {
     "qi4_gqa_decode_attention": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i64,
                                  _i64, _i64, ctypes.c_float, _p],
     "qi4_bf16_gemv_argmax": [_p, _p, _i64, _i64, _i64, _p, _p, _p],
+    "qi4_add_rmsnorm": [_p, _p, _i, _p, _p, _i64, _i64, ctypes.c_float, _p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }

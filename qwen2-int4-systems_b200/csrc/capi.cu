@@ -76,6 +76,12 @@ int current_device(DeviceInfo& info) {
 // process that calls cudaDeviceReset must not use the FP32-activation paths
 // on that device afterwards).
 cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t stream) {
+  // Under stream capture, allocate from the device's default stream-ordered
+  // allocator: the graph turns it into its own allocation node.
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusActive)
+    return cudaMallocAsync(p, bytes, stream);
+  cudaGetLastError();
   static std::mutex mu;
   static cudaMemPool_t pools[64] = {};
   int dev = 0;

@@ -1,0 +1,62 @@
+"""Graph-captured decoding (engine.DecodeEngine) against the reference model.
+
+The engine's greedy tokens are checked teacher-forced: the reference model
+(b200 backend, its own attention) runs the full forward over the engine's
+generated sequence, and at every generated position whose top-1/top-2 logit
+gap exceeds 0.05 the engine must have picked the reference's argmax (random-
+init models have near-ties where FP32 summation order alone decides). Batches
+of 2 (GEMV path, fused lm_head argmax, left padding), 1 (the full Qwen2-1.5B)
+and 12 (tensor-core linears, matmul lm_head); a second generate() on the same
+engine reuses the captured graph and returns the same tokens.
+"""
+
+import importlib
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_teacher_forced(model, seq, prompt_len, mask=None, gap=0.05, min_clear=3):
+    with torch.inference_mode():
+        full_mask = None if mask is None else torch.cat(
+            (mask, torch.ones(seq.shape[0], seq.shape[1] - mask.shape[1], dtype=mask.dtype, device=mask.device)),
+            dim=1)
+        logits = model(seq, attention_mask=full_mask)[:, prompt_len - 1:-1].float()
+    chosen = seq[:, prompt_len:]
+    top2 = logits.topk(2, dim=-1).values
+    clear = (top2[..., 0] - top2[..., 1]) > gap
+    agree = logits.argmax(-1) == chosen
+    assert int(clear.sum()) >= min_clear
+    assert bool(agree[clear].all()), (agree, clear)
+
+
+@pytest.mark.parametrize("batch", [2, 12])
+def test_engine_small_model_matches_reference(b200, cuda_device, batch):
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    eng_mod = importlib.import_module(b200.__name__ + ".engine")
+    cfg = q2.qwen2_config(num_hidden_layers=2, vocab_size=512)
+    model = q2.build_random_qwen2(cfg, device=cuda_device, seed=11)
+    prompt = torch.randint(0, 512, (batch, 9), generator=torch.Generator().manual_seed(batch)).to(cuda_device)
+    mask = torch.ones(batch, 9, dtype=torch.bool, device=cuda_device)
+    mask[1, :4] = False  # left padding
+    engine = eng_mod.DecodeEngine(model, batch=batch, max_len=32)
+    seq = engine.generate(prompt, 12, attention_mask=mask)
+    assert seq.shape == (batch, 21) and torch.equal(seq[:, :9], prompt)
+    _check_teacher_forced(model, seq, 9, mask)
+    again = engine.generate(prompt, 12, attention_mask=mask)
+    assert torch.equal(again, seq)
+    lib = importlib.import_module(b200.__name__ + "._lib").load()
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_engine_full_qwen2_batch1(b200, cuda_device):
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    eng_mod = importlib.import_module(b200.__name__ + ".engine")
+    model = q2.build_random_qwen2(device=cuda_device, seed=0)
+    prompt = torch.randint(0, model.config.vocab_size, (1, 32),
+                           generator=torch.Generator().manual_seed(20260831)).to(cuda_device)
+    engine = eng_mod.DecodeEngine(model, batch=1, max_len=64)
+    seq = engine.generate(prompt, 16)
+    _check_teacher_forced(model, seq, 32)
