@@ -18,12 +18,16 @@
 //
 // Work split ("flash decoding"): a CTA owns one (batch, KV head, 64-key
 // split) and all G query heads of that KV head, so K and V are read once for
-// the group (no expansion). 4 warps take 16 keys each, 8 at a time: lane
-// (key kk = lane / 4, quarter dq = lane % 4) dots its 32 dims of the key with
-// the G queries (held in shared memory, FP32), a 2-step shuffle sums the
-// quarters; per head an online softmax (running max, rescaled sums) and
-// P.V with lane = 4 output dims. The CTA's partial (max, sum, 128 sums per
-// head) goes to scratch; a second kernel combines the splits per head.
+// the group (no expansion). The split's keys and values are copied into
+// shared memory (asynchronous 16-byte copies, all in flight while the queries
+// are rotated), rows padded so that the reads below are conflict-free. 4
+// warps take 16 keys each, 8 at a time: lane (key kk = lane % 8, quarter
+// dq = lane / 8) dots its 32 dims of the key with the G queries (held in
+// shared memory, FP32), a 2-step shuffle sums the quarters; per head an
+// online softmax (running max, rescaled sums) and P.V with lane = 4 output
+// dims. The CTA's partial (max, sum, 128 sums per head) goes to scratch; a
+// second kernel combines the splits per head. Both launch as programmatic
+// dependents (the next kernel's prologue overlaps this one's tail).
 #include <algorithm>
 #include <cmath>
 
@@ -60,6 +64,7 @@ struct AttnArgs {
 };
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ uint32_t smem_addr_u(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // RoPE of element d of a head vector x (bf16 roundings as the reference's
@@ -70,22 +75,46 @@ __device__ __forceinline__ float rope(const __nv_bfloat16* x, const __nv_bfloat1
   return rbf(rbf(xd * bf(c[d])) + rbf(rh * bf(s[d])));
 }
 
+constexpr int kRowBytes = kD * 2 + 16;  // a staged key / value row, padded (conflict-free 16-byte reads)
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
 __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs a) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // Programmatic dependent launch: the next kernel may start its prologue;
+  // this one waits for its predecessor (the q/k/v projections) first.
+  pdl_launch_dependents();
+  pdl_wait();
   const int L = a.lengths[b];  // past keys; the new one is key L
   const int nkeys = L + 1;
   const int k0 = split * kSplitKeys;
-  if (k0 >= nkeys || L >= a.cap) return;  // nothing of this sequence here (or no room: host-checked)
+  if (k0 >= nkeys || L >= a.cap) return;  // nothing of this sequence here (or no room)
   const int k1 = min(nkeys, k0 + kSplitKeys);
   const int G = a.G;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  __shared__ __align__(16) float q_s[kMaxGroup][4][kQPad];  // RoPE'd queries, FP32, by head and quarter
-  __shared__ float p_s[kWarps][8][kMaxGroup];          // softmax weights of a warp's 8 keys
-  __shared__ float knew_s[kD], vnew_s[kD];             // the new key (RoPE'd) and value
+  __shared__ __align__(16) uint8_t kv_s[2][kSplitKeys][kRowBytes];  // past keys / values of the split
+  __shared__ __align__(16) float q_s[kMaxGroup][4][kQPad];          // RoPE'd queries, FP32, by head and quarter
+  __shared__ float p_s[kWarps][8][kMaxGroup];                       // softmax weights of a warp's 8 keys
   __shared__ float red_m[kWarps][kMaxGroup], red_l[kWarps][kMaxGroup];
-  __shared__ float red_acc[kWarps][kMaxGroup][kD];
+  // After the key loop the staged rows are dead: the warps' partial sums reuse them.
+  static_assert(sizeof(float) * kWarps * kMaxGroup * kD <= sizeof(uint8_t) * 2 * kSplitKeys * kRowBytes, "");
+  auto red_acc = reinterpret_cast<float (*)[kMaxGroup][kD]>(&kv_s[0][0][0]);
 
+  // 1. The split's past keys and values: all copies in flight at once.
+  const __nv_bfloat16* kbase = a.k_cache + b * a.cb + kvh * a.ch;
+  const __nv_bfloat16* vbase = a.v_cache + b * a.cb + kvh * a.ch;
+  const int npast = min(k1, L) - k0;  // keys k0 .. min(k1, L) - 1 come from the cache
+  for (int i = tid; i < npast * 16; i += blockDim.x) {
+    const int r = i >> 4, c = i & 15;
+    cp_async16(smem_addr_u(&kv_s[0][r][c * 16]), kbase + (int64_t)(k0 + r) * kD + c * 8);
+    cp_async16(smem_addr_u(&kv_s[1][r][c * 16]), vbase + (int64_t)(k0 + r) * kD + c * 8);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
+  // 2. Meanwhile: RoPE of the queries, and of the new key if it is in this split.
   const __nv_bfloat16* cs = nullptr;
   const __nv_bfloat16* sn = nullptr;
   if (a.cos) {
@@ -96,27 +125,30 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
   for (int i = tid; i < G * kD; i += blockDim.x) {
     const int h = i / kD, d = i - h * kD;
     const __nv_bfloat16* qh = a.q + ((int64_t)b * a.Hq + kvh * G + h) * kD;
-    const float v = cs ? rope(qh, cs, sn, d) : bf(qh[d]);
-    q_s[h][d >> 5][d & 31] = v;
+    q_s[h][d >> 5][d & 31] = cs ? rope(qh, cs, sn, d) : bf(qh[d]);
   }
   const bool has_new = k0 <= L && L < k1;
   if (has_new) {
-    // The new key / value: used from here, and appended to the cache.
+    // The new key / value: staged as row L - k0, and appended to the cache.
     const __nv_bfloat16* kn = a.k_new + ((int64_t)b * a.Hkv + kvh) * kD;
     const __nv_bfloat16* vn = a.v_new + ((int64_t)b * a.Hkv + kvh) * kD;
     __nv_bfloat16* kc = a.k_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
     __nv_bfloat16* vc = a.v_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
+    __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(&kv_s[0][L - k0][0]);
+    __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(&kv_s[1][L - k0][0]);
     for (int d = tid; d < kD; d += blockDim.x) {
-      const float kv = cs ? rope(kn, cs, sn, d) : bf(kn[d]);
-      knew_s[d] = kv;
-      vnew_s[d] = bf(vn[d]);
-      kc[d] = __float2bfloat16_rn(kv);  // exact: kv is a bf16 value
+      const __nv_bfloat16 kv = cs ? __float2bfloat16_rn(rope(kn, cs, sn, d)) : kn[d];
+      ks[d] = kv;
+      vs[d] = vn[d];
+      kc[d] = kv;
       vc[d] = vn[d];
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
-  const int kk = lane >> 2, dq = lane & 3;
+  // 3. Keys 8 at a time per warp: lane (key kk = lane % 8, quarter dq = lane / 8).
+  const int kk = lane & 7, dq = lane >> 3;
   float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][4];
 #pragma unroll
   for (int h = 0; h < kMaxGroup; ++h) {
@@ -125,12 +157,8 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
   }
-  const __nv_bfloat16* kbase = a.k_cache + b * a.cb + kvh * a.ch;
-  const __nv_bfloat16* vbase = a.v_cache + b * a.cb + kvh * a.ch;
   const uint8_t* mrow = a.key_mask ? a.key_mask + (int64_t)b * a.mask_stride : nullptr;
-
   for (int g0 = k0 + warp * 8; g0 < k1; g0 += kWarps * 8) {
-    // Scores of this lane's key (kk) over its 32 dims for every head.
     const int key = g0 + kk;
     const bool valid = key < k1 && (!mrow || mrow[key] != 0);
     float s[kMaxGroup];
@@ -138,20 +166,15 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     for (int h = 0; h < kMaxGroup; ++h) s[h] = 0.f;
     if (key < k1) {
       float kf[32];
-      if (key == L && has_new) {
+      const uint4* kp = reinterpret_cast<const uint4*>(&kv_s[0][key - k0][dq * 64]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) kf[j] = knew_s[dq * 32 + j];
-      } else {
-        const uint4* kp = reinterpret_cast<const uint4*>(kbase + (int64_t)key * kD + dq * 32);
+      for (int c = 0; c < 4; ++c) {
+        const uint4 w = kp[c];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 w = kp[c];
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            kf[c * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
-            kf[c * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
-          }
+        for (int e = 0; e < 4; ++e) {
+          kf[c * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
+          kf[c * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
         }
       }
 #pragma unroll
@@ -173,8 +196,8 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     }
 #pragma unroll
     for (int h = 0; h < kMaxGroup; ++h) {
-      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
-      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 8);
+      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 16);
       s[h] = valid ? s[h] * a.scale : -INFINITY;
     }
     // Online softmax over this group of 8 keys, per head.
@@ -182,9 +205,9 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     for (int h = 0; h < kMaxGroup; ++h) {
       if (h >= G) continue;
       float mx = s[h];
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float mn = fmaxf(m[h], mx);
       const float alpha = mn == -INFINITY ? 1.f : __expf(m[h] - mn);
       const float p = s[h] == -INFINITY ? 0.f : __expf(s[h] - mn);
@@ -200,17 +223,9 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     for (int e = 0; e < 8; ++e) {
       const int key2 = g0 + e;
       if (key2 >= k1) break;
-      float vf[4];
-      if (key2 == L && has_new) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) vf[j] = vnew_s[lane * 4 + j];
-      } else {
-        const uint2 w = *reinterpret_cast<const uint2*>(vbase + (int64_t)key2 * kD + lane * 4);
-        vf[0] = __uint_as_float(w.x << 16);
-        vf[1] = __uint_as_float(w.x & 0xFFFF0000u);
-        vf[2] = __uint_as_float(w.y << 16);
-        vf[3] = __uint_as_float(w.y & 0xFFFF0000u);
-      }
+      const uint2 w = *reinterpret_cast<const uint2*>(&kv_s[1][key2 - k0][lane * 8]);
+      const float vf[4] = {__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u),
+                           __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xFFFF0000u)};
 #pragma unroll
       for (int h = 0; h < kMaxGroup; ++h) {
         if (h >= G) continue;
@@ -221,14 +236,15 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     }
     __syncwarp();
   }
+  __syncthreads();  // every warp is done with the staged rows
   // Per warp: sum l over the 8 key lanes (each value is replicated 4 times).
 #pragma unroll
   for (int h = 0; h < kMaxGroup; ++h) {
     if (h >= G) continue;
     float t = l[h];
+    t += __shfl_xor_sync(0xffffffffu, t, 1);
+    t += __shfl_xor_sync(0xffffffffu, t, 2);
     t += __shfl_xor_sync(0xffffffffu, t, 4);
-    t += __shfl_xor_sync(0xffffffffu, t, 8);
-    t += __shfl_xor_sync(0xffffffffu, t, 16);
     if (lane == 0) {
       red_m[warp][h] = m[h];
       red_l[warp][h] = t;
@@ -260,12 +276,13 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
   }
 }
 
-// out[b, h * D + d] = sum_s e^(m_s - M) acc_s[d] / sum_s e^(m_s - M) l_s.
 // A sequence whose cache is full (L_b >= cap) was not processed: its output
 // is zero (and qi4_device_status reports QI4_DEVICE_CACHE_FULL).
 __global__ void gqa_combine_kernel(const float* __restrict__ partial, const int32_t* __restrict__ lengths,
                                    __nv_bfloat16* __restrict__ out, int Hkv, int G, int splits, int cap) {
   const int h = blockIdx.x, b = blockIdx.y;  // query head
+  pdl_launch_dependents();
+  pdl_wait();
   const int kvh = h / G, hg = h - kvh * G;
   const int L = lengths[b];
   if (L >= cap) {
@@ -319,12 +336,21 @@ cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_ne
   a.cap = cap;
   a.splits = attention_splits(cap);
   a.scale = scale;
-  gqa_decode_kernel<<<dim3(a.splits, Hkv, B), kWarps * 32, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, Hkv, B);
+  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_decode_kernel, a);
   if (e != cudaSuccess) return e;
-  gqa_combine_kernel<<<dim3(Hq, B), kD, 0, stream>>>(partial, lengths, static_cast<__nv_bfloat16*>(out), Hkv, a.G,
-                                                     a.splits, cap);
-  return cudaGetLastError();
+  cfg.gridDim = dim3(Hq, B, 1);
+  cfg.blockDim = dim3(kD, 1, 1);
+  return cudaLaunchKernelEx(&cfg, gqa_combine_kernel, static_cast<const float*>(partial), lengths,
+                            static_cast<__nv_bfloat16*>(out), Hkv, a.G, a.splits, cap);
 }
 
 int read_attention_error(cudaStream_t stream) {

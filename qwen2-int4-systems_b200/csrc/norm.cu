@@ -6,7 +6,8 @@
 //   h   = bf16(h + bf16(delta))                       (delta bf16 or FP32)
 //   out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w)   (FP32 statistics)
 // Both in one pass over the row: h is updated in place (delta may be NULL:
-// normalisation only).
+// normalisation only). Launched as a programmatic dependent of the kernel
+// before it (which produced delta).
 #include "qi4_common.cuh"
 
 namespace qi4 {
@@ -21,6 +22,8 @@ __global__ void __launch_bounds__(kThreads) add_rmsnorm_kernel(__nv_bfloat16* __
                                                                const __nv_bfloat16* __restrict__ w,
                                                                __nv_bfloat16* __restrict__ out, int D, float eps) {
   const int row = blockIdx.x, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();  // delta is the previous kernel's output
   __nv_bfloat16* hr = h + (int64_t)row * D;
   float v[kMaxPerThread];
   float ss = 0.f;
@@ -80,8 +83,23 @@ extern "C" QI4_API int qi4_add_rmsnorm(void* h, const void* delta, int delta_dty
     set_error("delta dtype %d is not BF16 or F32", delta_dtype);
     return QI4_ERR_DTYPE;
   }
-  add_rmsnorm_kernel<<<(unsigned)B, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(h), delta, delta_dtype, static_cast<const __nv_bfloat16*>(weight),
-      static_cast<__nv_bfloat16*>(out), (int)D, eps);
+  // A programmatic dependent launch: the kernel's prologue overlaps the tail
+  // of the kernel before it, and it waits for that kernel before reading.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)B, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, static_cast<__nv_bfloat16*>(h), delta, delta_dtype,
+                     static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), (int)D, eps);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("add_rmsnorm launch failed: %s", cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
   return launch_status("add_rmsnorm");
 }
