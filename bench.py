@@ -1,20 +1,36 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 W4G64 QuantLinear forward (decode GEMV headline).
+"""Benchmark of the B200 W4G64 QuantLinear forward and the decode built on it.
 
-Workload (the seven-shape sweep at M=1, i.e. one decode token through every
-quantised linear of Qwen2-1.5B): the seven linear shapes q 1536->1536,
-k/v 1536->256, o 1536->1536, gate/up 1536->8960, down 8960->1536, for each
-of the 28 layers, symmetric W4G64 RTN of bf16 weights ~N(0, 0.02), bf16
-activations ~N(0, 1), q/k/v with bf16 bias. A step is one pass over all 196
-linears; the 655 MB of packed weights per step are far larger than L2, so no
-flush is needed. Synthetic, seeded data (no checkpoint is used).
+Headline workload: one decode token (M = 1) through every quantised linear of
+Qwen2-1.5B's 28 layers, as the decode engine runs them: per layer q/k/v in
+one grouped launch, o_proj on q_proj's output (the attention stand-in),
+gate/up fused with SwiGLU on o_proj's output (FP32 out), down_proj on that
+FP32 tensor (FP32 out). Symmetric W4G64 RTN of bf16 weights ~N(0, 0.02),
+bf16 activations ~N(0, 1), q/k/v with bf16 bias. 112 launches per step,
+captured once in a CUDA graph of C-ABI calls (programmatic dependent launch
+between them) and replayed K times; the 655 MB of packed weights per step
+are far larger than L2, so no flush is needed. Synthetic, seeded data (no
+checkpoint is used).
 
-  value  = algorithmic bytes per step (N*K/2 + 2*N*K/64 + 2*M*K + 2*M*N per linear, + 2*N with bias) / device time,
-           step captured once in a CUDA graph of C-ABI launches, replayed K times
-  e2e    = same metric through the public Python API (b200_w4g64_linear) with
-           the step's activations copied host->device and outputs device->host
-           inside the timed region
-  gemm   = the seven shapes at M=2048 (TFLOP/s), tensor-core kernel
+  value   = algorithmic bytes per step (per launch: N*K/2 packed weights +
+            2*N*K/64 scales (+2*N bias) + x + outputs, at their dtypes) /
+            device time of the step, summed over ranks (replicas)
+  e2e     = the same step through the public Python API (b200_w4g64_linear_multi,
+            b200_w4g64_linear, b200_w4g64_gate_up_silu), captured once as a
+            user would, with the step's activations copied host->device and
+            its outputs device->host inside the timed region
+  variants: the 196 single-linear launches, the bf16 grouped step, the
+            persistent chain (one cooperative launch per step)
+  gemm    = the seven shapes at M = 2048 (TFLOP/s), tensor-core kernel; q/k/v
+            also as one grouped call
+  serving = the decode engine on the reference model: config 3 (batch 1,
+            512-token prompt, 128 greedy steps) and config 4 (batch 64,
+            1024-token prompts, 256 steps), tok/s; per rank (replicas) at N > 1
+  qwen2_decode = the reference harness (greedy_generate_cached) on the b200
+            backend, with the final-logits cosine against the reference torch
+            backend
+  split_prefill_mlp = the M = 4096 MLP unsplit on one GPU (N = 1) or split over
+            the ranks (column / column_row), with an output check
   roofline, cpu_baseline, clocks: see the JSON keys.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
@@ -33,6 +49,7 @@ import sys
 import threading
 import time
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 import torch
@@ -48,17 +65,23 @@ LAYERS = 28
 SHAPES = [("q", 1536, 1536, True), ("k", 1536, 256, True), ("v", 1536, 256, True),
           ("o", 1536, 1536, False), ("gate", 1536, 8960, False), ("up", 1536, 8960, False),
           ("down", 8960, 1536, False)]
-WORKLOAD = "qwen2-1.5b-7-linears-x28-layers-w4g64-rtn-m1"
+WORKLOAD = "qwen2-1.5b-decode-linears-x28-layers-w4g64-rtn-m1"
+F32, BF16 = 2, 1  # C-ABI dtype codes (include/qi4_b200.h)
 
 
-def alg_bytes(m: int, n: int, k: int, bias: bool, asym: bool = False) -> int:
-    """Algorithmic bytes of one linear: packed weights + fp16 scales + x + out (+zeros, +bias)."""
-    b = n * k // 2 + n * (k // 64) * 2 + m * k * 2 + m * n * 2
+def weight_bytes(n: int, k: int, bias: bool = False, asym: bool = False) -> int:
+    """Packed weights + fp16 scales (+ packed zero points) (+ bf16 bias) of one linear."""
+    b = n * k // 2 + n * (k // 64) * 2
     if asym:
         b += (n * (k // 64) + 1) // 2
     if bias:
         b += 2 * n
     return b
+
+
+def alg_bytes(m: int, n: int, k: int, bias: bool, asym: bool = False, x_size: int = 2, out_size: int = 2) -> int:
+    """Algorithmic bytes of one linear: weights + scales (+zeros, +bias) + x + out."""
+    return weight_bytes(n, k, bias, asym) + m * k * x_size + m * n * out_size
 
 
 # ---------------------------------------------------------------------------
@@ -73,7 +96,7 @@ class ClockSampler:
         "display_clock_setting": 0x100,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.samples: list[tuple[int, int]] = []
         self.period = period_s
         self.handle = None
@@ -155,12 +178,92 @@ def build_model_weights(device, seed: int = 0) -> list[list[dict]]:
     return layers
 
 
+def as_module(e: dict) -> SimpleNamespace:
+    """A QuantLinear-like view of one bench weight (for the Python API)."""
+    return SimpleNamespace(qweight=e["qweight"], scales=e["scales"], zeros=e["zeros"], bias=e["bias"],
+                           in_features=e["k"], out_features=e["n"], group_size=64, packing="canonical")
+
+
 # ---------------------------------------------------------------------------
 # device-side measurement through the C ABI
 # ---------------------------------------------------------------------------
 
+def capture(launch) -> torch.cuda.CUDAGraph:
+    """Warm `launch` up on a side stream, then capture one call in a graph."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        launch()
+        launch()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        launch()
+    return g
+
+
+def _arr(vals):
+    return (ctypes.c_void_p * len(vals))(*vals)
+
+
+class DecodeStep:
+    """The headline step: per layer q/k/v grouped (qi4_w4g64_linear_multi),
+    o_proj on q's output (qi4_w4g64_linear_ex), gate/up + SwiGLU on o's output
+    (qi4_w4g64_gate_up_silu, FP32 out), down_proj on that FP32 tensor (FP32
+    out). 4 launches per layer, each reading the previous launch's output."""
+
+    def __init__(self, lib, layers: list[list[dict]], device, gen: torch.Generator):
+        self.lib, self.layers = lib, []
+        self.nbytes = 0
+        for layer in layers:
+            by = {e["name"]: e for e in layer}
+            x = torch.randn(1, 1536, device=device, generator=gen).to(torch.bfloat16)
+            q, k, v = (torch.empty(1, by[n]["n"], device=device, dtype=torch.bfloat16) for n in "qkv")
+            o = torch.empty(1, 1536, device=device, dtype=torch.bfloat16)
+            h = torch.empty(1, 8960, device=device, dtype=torch.float32)
+            y = torch.empty(1, 1536, device=device, dtype=torch.float32)
+            self.layers.append(SimpleNamespace(by=by, x=x, q=q, k=k, v=v, o=o, h=h, y=y))
+            self.nbytes += 1536 * 2 + sum(weight_bytes(by[n]["n"], 1536, True) + by[n]["n"] * 2 for n in "qkv")
+            self.nbytes += alg_bytes(1, 1536, 1536, False)
+            self.nbytes += 2 * weight_bytes(8960, 1536) + 1536 * 2 + 8960 * 4
+            self.nbytes += alg_bytes(1, 1536, 8960, False, x_size=4, out_size=4)
+        self.launches_per_step = 4 * len(layers)
+
+    def launch(self):
+        lib, stream = self.lib, torch.cuda.current_stream().cuda_stream
+        for L in self.layers:
+            b = L.by
+            qkv = [b["q"], b["k"], b["v"]]
+            rc = lib.qi4_w4g64_linear_multi(
+                L.x.data_ptr(), BF16, 1, 1536, 3, _arr([e["qweight"].data_ptr() for e in qkv]),
+                _arr([e["scales"].data_ptr() for e in qkv]), _arr([e["zeros"].data_ptr() for e in qkv]),
+                _arr([e["bias"].data_ptr() for e in qkv]), BF16,
+                _arr([L.q.data_ptr(), L.k.data_ptr(), L.v.data_ptr()]), (ctypes.c_int64 * 3)(*[e["n"] for e in qkv]),
+                stream)
+            o = b["o"]
+            rc = rc or lib.qi4_w4g64_linear_ex(L.q.data_ptr(), BF16, 1, 1536, o["qweight"].data_ptr(),
+                                               o["scales"].data_ptr(), o["zeros"].data_ptr(), None, -1,
+                                               L.o.data_ptr(), 1536, stream, 0, 1)
+            g, u = b["gate"], b["up"]
+            rc = rc or lib.qi4_w4g64_gate_up_silu(L.o.data_ptr(), BF16, 1, 1536, g["qweight"].data_ptr(),
+                                                  g["scales"].data_ptr(), g["zeros"].data_ptr(),
+                                                  u["qweight"].data_ptr(), u["scales"].data_ptr(),
+                                                  u["zeros"].data_ptr(), L.h.data_ptr(), 8960, stream)
+            d = b["down"]
+            rc = rc or lib.qi4_w4g64_linear_ex(L.h.data_ptr(), F32, 1, 8960, d["qweight"].data_ptr(),
+                                               d["scales"].data_ptr(), d["zeros"].data_ptr(), None, -1,
+                                               L.y.data_ptr(), 1536, stream, 0, 1)
+            if rc:
+                raise RuntimeError(f"decode-step launch failed: {rc}")
+
+    def graph(self):
+        return capture(self.launch)
+
+
 class Chain:
-    """A list of C-ABI launches with preallocated activations and outputs."""
+    """A list of single-linear C-ABI launches (bf16 in and out) with
+    preallocated activations and outputs."""
 
     def __init__(self, lib, entries: list[dict], m: int, device, gen: torch.Generator, algo: int = 0):
         self.lib, self.entries, self.m, self.algo = lib, entries, m, algo
@@ -172,24 +275,14 @@ class Chain:
         for e, x, o in zip(self.entries, self.x, self.out):
             b = e["bias"]
             rc = self.lib.qi4_w4g64_linear_ex(
-                x.data_ptr(), 1, self.m, e["k"], e["qweight"].data_ptr(), e["scales"].data_ptr(),
-                e["zeros"].data_ptr(), None if b is None else b.data_ptr(), -1 if b is None else 1,
+                x.data_ptr(), BF16, self.m, e["k"], e["qweight"].data_ptr(), e["scales"].data_ptr(),
+                e["zeros"].data_ptr(), None if b is None else b.data_ptr(), -1 if b is None else BF16,
                 o.data_ptr(), e["n"], stream, self.algo, 1)
             if rc:
                 raise RuntimeError(f"launch failed: {rc}")
 
     def graph(self) -> torch.cuda.CUDAGraph:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            self.launch()
-            self.launch()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.launch()
-        return g
+        return capture(self.launch)
 
     def bytes(self) -> int:
         return sum(alg_bytes(self.m, e["n"], e["k"], e["bias"] is not None) for e in self.entries)
@@ -199,41 +292,44 @@ class Chain:
 
 
 class GroupedChain:
-    """The decode step with the linears that share an input grouped into one
-    C-ABI launch (qi4_w4g64_linear_multi): per layer q/k/v, o, gate/up, down
-    (4 launches instead of 7). Same weights, same bytes, same outputs."""
+    """The bf16 decode step with the linears that share an input grouped into
+    one C-ABI launch (qi4_w4g64_linear_multi): per layer q/k/v, o, gate/up,
+    down (4 launches instead of 7), independent inputs."""
 
     GROUPS = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
 
-    def __init__(self, lib, layers: list[list[dict]], device, gen: torch.Generator):
-        self.lib = lib
+    def __init__(self, lib, layers: list[list[dict]], device, gen: torch.Generator, m: int = 1):
+        self.lib, self.m = lib, m
         self.launches = []
+        self.nbytes = 0
         for layer in layers:
             by_name = {e["name"]: e for e in layer}
             for group in self.GROUPS:
                 ents = [by_name[n] for n in group]
                 k = ents[0]["k"]
-                x = torch.randn(1, k, device=device, generator=gen).to(torch.bfloat16)
-                outs = [torch.empty(1, e["n"], device=device, dtype=torch.bfloat16) for e in ents]
+                x = torch.randn(m, k, device=device, generator=gen).to(torch.bfloat16)
+                outs = [torch.empty(m, e["n"], device=device, dtype=torch.bfloat16) for e in ents]
                 c = len(ents)
-                arr = lambda vals: (ctypes.c_void_p * c)(*vals)
                 bias = [e["bias"] for e in ents]
-                self.launches.append((x, outs, c, k, arr([e["qweight"].data_ptr() for e in ents]),
-                                      arr([e["scales"].data_ptr() for e in ents]),
-                                      arr([e["zeros"].data_ptr() for e in ents]),
-                                      arr([None if b is None else b.data_ptr() for b in bias]),
-                                      1 if any(b is not None for b in bias) else -1,
-                                      arr([o.data_ptr() for o in outs]),
+                self.launches.append((x, outs, c, k, _arr([e["qweight"].data_ptr() for e in ents]),
+                                      _arr([e["scales"].data_ptr() for e in ents]),
+                                      _arr([e["zeros"].data_ptr() for e in ents]),
+                                      _arr([None if b is None else b.data_ptr() for b in bias]),
+                                      BF16 if any(b is not None for b in bias) else -1,
+                                      _arr([o.data_ptr() for o in outs]),
                                       (ctypes.c_int64 * c)(*[e["n"] for e in ents])))
+                self.nbytes += m * k * 2 + sum(weight_bytes(e["n"], k, e["bias"] is not None) + m * e["n"] * 2
+                                               for e in ents)
 
     def launch(self):
         stream = torch.cuda.current_stream().cuda_stream
         for x, outs, c, k, qw, sc, z, b, bd, o, ns in self.launches:
-            rc = self.lib.qi4_w4g64_linear_multi(x.data_ptr(), 1, 1, k, c, qw, sc, z, b, bd, o, ns, stream)
+            rc = self.lib.qi4_w4g64_linear_multi(x.data_ptr(), BF16, self.m, k, c, qw, sc, z, b, bd, o, ns, stream)
             if rc:
                 raise RuntimeError(f"grouped launch failed: {rc}")
 
-    graph = Chain.graph
+    def graph(self):
+        return capture(self.launch)
 
 
 def time_graph(g: torch.cuda.CUDAGraph, reps: int, warmup: int) -> float:
@@ -250,19 +346,21 @@ def time_graph(g: torch.cuda.CUDAGraph, reps: int, warmup: int) -> float:
     return start.elapsed_time(end) / reps
 
 
+def max_over_ranks(dist, value: float, device) -> float:
+    if not dist:
+        return value
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's torch backend restated (oracle/torch_port.py)
 # ---------------------------------------------------------------------------
 
-def cpu_linear_sample(reps: int = 3, sample: str = "layer") -> dict:
-    from oracle import torch_port
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    gen = torch.Generator().manual_seed(1)
-    shapes = SHAPES if sample == "layer" else [s for s in SHAPES if s[0] == "gate"]
+def _cpu_layer(gen: torch.Generator):
     data = []
-    for name, k, n, has_bias in shapes:
+    for name, k, n, has_bias in SHAPES:
         w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).float().view(n, k // 64, 64)
         s = w.abs().amax(-1) / 7.0
         s = torch.where(s == 0, torch.ones_like(s), s)
@@ -272,6 +370,15 @@ def cpu_linear_sample(reps: int = 3, sample: str = "layer") -> dict:
         bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16) if has_bias else None
         x = torch.randn(1, k, generator=gen).to(torch.bfloat16)
         data.append((x, qw, s.to(torch.float16), z, bias, n, k))
+    return data
+
+
+def cpu_linear_sample(reps: int = 3) -> dict:
+    from oracle import torch_port
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    data = _cpu_layer(torch.Generator().manual_seed(1))
 
     def run():
         for x, qw, sc, z, bias, n, k in data:
@@ -286,8 +393,8 @@ def cpu_linear_sample(reps: int = 3, sample: str = "layer") -> dict:
     nbytes = sum(alg_bytes(1, n, k, bias is not None) for _, _, _, _, bias, n, k in data)
     t = statistics.median(times)
     return {"value": nbytes / t / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(data)} linear(s) of one layer at M=1 ({sample}), median of {reps}, "
-                      f"oracle/torch_port.py (reference torch backend restated) on {threads} threads",
+            "sample": f"one layer's 7 linears at M=1, median of {reps}, oracle/torch_port.py "
+                      f"(reference torch backend restated) on {threads} threads",
             "seconds_per_sample": t}
 
 
@@ -295,23 +402,11 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import torch_port  # noqa: F401  (fails loudly if the oracle is missing)
+    from oracle import torch_port as tp  # fails loudly if the oracle is missing
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    gen = torch.Generator().manual_seed(1)
-    per_step = []
-    for name, k, n, has_bias in SHAPES:
-        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).float().view(n, k // 64, 64)
-        s = w.abs().amax(-1) / 7.0
-        s = torch.where(s == 0, torch.ones_like(s), s)
-        codes = torch.round(w / s.unsqueeze(-1)).clamp_(-7, 7).to(torch.int16).view(n, k)
-        qw = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).reshape(-1, 1)
-        z = torch.zeros((n * (k // 64) + 1) // 2, 1, dtype=torch.uint8)
-        bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16) if has_bias else None
-        per_step.append((torch.randn(1, k, generator=gen).to(torch.bfloat16), qw, s.to(torch.float16), z,
-                         bias, n, k))
-    from oracle import torch_port as tp
+    per_step = _cpu_layer(torch.Generator().manual_seed(1))
 
     def step():
         for x, qw, sc, z, bias, n, k in per_step:
@@ -338,19 +433,212 @@ def run_reference(args) -> None:
 
 
 # ---------------------------------------------------------------------------
-# main (our arm)
+# sections of our arm
 # ---------------------------------------------------------------------------
 
-def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
-    """Batch-1 decode: the reference's Qwen2-1.5B (random init, W4G64 RTN) on
-    the b200 backend, batch 1, greedy decode through the reference's own
-    ``greedy_generate_cached``; the same model on the reference's ``torch``
-    backend on this GPU for comparison (fewer steps). The ``b200_fused_mlp``
-    leg also routes the MLP through the fused gate/up SwiGLU call
-    (``register_with_reference(fuse_mlp=True)``)."""
+def step_variants(lib, layers, device, gen, dist) -> dict:
+    """The other ways to run the same decode linears: 196 single-linear
+    launches and the bf16 grouped step (independent inputs), and the
+    persistent chain (one cooperative launch of all 112 dependent stages)."""
+    out = {}
+    entries = [e for layer in layers for e in layer]
+    per = Chain(lib, entries, 1, device, gen)
+    t = max_over_ranks(dist, time_graph(per.graph(), reps=20, warmup=3), device)
+    out["per_linear"] = {"launches_per_step": len(entries), "ms_per_step": t, "GBps": per.bytes() / (t / 1e3) / 1e9,
+                         "api": "qi4_w4g64_linear_ex per linear, CUDA graph"}
+    grouped = GroupedChain(lib, layers, device, gen)
+    t = max_over_ranks(dist, time_graph(grouped.graph(), reps=20, warmup=3), device)
+    out["grouped_bf16"] = {"launches_per_step": len(grouped.launches), "ms_per_step": t,
+                           "GBps": grouped.nbytes / (t / 1e3) / 1e9,
+                           "api": "qi4_w4g64_linear_multi (q/k/v, gate/up bf16 grouped), CUDA graph"}
+    chain_mod = importlib.import_module(PACKAGE + ".chain")
+    mods = []
+    for layer in layers:
+        by = {e["name"]: as_module(e) for e in layer}
+        mods.append(SimpleNamespace(
+            self_attn=SimpleNamespace(q_proj=by["q"], k_proj=by["k"], v_proj=by["v"], o_proj=by["o"]),
+            mlp=SimpleNamespace(gate_proj=by["gate"], up_proj=by["up"], down_proj=by["down"])))
+    x = torch.randn(1, 1536, device=device, generator=gen).to(torch.bfloat16)
+    stages, _ = chain_mod.decoder_linear_stages(mods, x)
+    chain = chain_mod.DecodeChain(stages, 1)
+    info = chain.info()
+    t = max_over_ranks(dist, time_graph(capture(chain.run), reps=20, warmup=3), device)
+    out["chain"] = {"launches_per_step": 1, "ms_per_step": t, "GBps": info["alg_bytes"] / (t / 1e3) / 1e9,
+                    "ctas": info["ctas"], "prepacked_bytes": info["prepacked_bytes"],
+                    "api": "qi4_chain_run (persistent cooperative kernel, prepacked weights)"}
+    chain.close()
+    return out
+
+
+def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
+    """Secondary figures for the workloads the headline does not cover:
+    config 0 (gate, symmetric, M = 1/4/16), config 1's other M points
+    (8/32/128/512, the seven shapes of all 28 layers: 655 MB rotated, > 5x
+    L2), config 2 (AWQ-style asymmetric down_proj, M = 1/16/2048, 40 distinct
+    matrices: 280 MB rotated, > 2x L2) and the 196 linears at M = 64 (the
+    linear part of config 4's decode step; the whole step is under
+    ``serving``). Library-chosen kernels (GEMV up to M = 16, tensor cores
+    above), CUDA graphs of C-ABI launches."""
+    q2 = importlib.import_module(PACKAGE + ".qwen2")
+    out = {}
+
+    def run(chain, reps=10):
+        t = time_graph(chain.graph(), reps=reps, warmup=3)
+        return t, chain.bytes() / (t / 1e3) / 1e9, chain.flops() / (t / 1e3) / 1e12
+
+    gates = [layer[4] for layer in layers]
+    out["cfg0_gate_sym_GBps"] = {f"m{m}": round(run(Chain(lib, gates, m, device, gen))[1], 1) for m in (1, 4, 16)}
+    sweep = {}
+    everything = [e for layer in layers for e in layer]
+    for m in (8, 32, 128, 512):
+        t, gbps, tf = run(Chain(lib, everything, m, device, gen), reps=5)
+        sweep[f"m{m}"] = {"GBps": round(gbps, 1), "TFLOPs": round(tf, 2), "ms_28_layers": round(t, 4)}
+    out["cfg1_seven_shapes"] = sweep
+    # Config 2: per-input-channel scaled weights, asymmetric RTN, activations divided by the channel scale.
+    chan = torch.exp(torch.empty(8960, device=device).uniform_(float(np.log(0.5)), float(np.log(2.0)), generator=gen))
+    downs = []
+    for _ in range(40):
+        w = torch.randn(1536, 8960, device=device, generator=gen) * 0.02 * chan
+        qw, sc, z = q2.quantize_asymmetric_rtn_torch(w.to(torch.bfloat16).float())
+        downs.append({"name": "down_awq", "k": 8960, "n": 1536, "qweight": qw, "scales": sc, "zeros": z, "bias": None})
+    cfg2 = {"matrices": len(downs), "rotated_MB": round(len(downs) * weight_bytes(1536, 8960, asym=True) / 1e6, 1)}
+    for m in (1, 16, 2048):
+        chain = Chain(lib, downs if m <= 16 else downs[:4], m, device, gen)
+        chain.x = [(x.float() / chan).to(torch.bfloat16) for x in chain.x]
+        t, _, tf = run(chain)
+        nbytes = sum(alg_bytes(m, 1536, 8960, False, asym=True) for _ in chain.entries)
+        cfg2[f"m{m}"] = {"GBps": round(nbytes / (t / 1e3) / 1e9, 1)} if m <= 16 else \
+            {"TFLOPs": round(tf, 1), "frac_of_bf16_peak": round(tf / tensor_peak, 3)}
+    out["cfg2_awq_down"] = cfg2
+    t, gbps, tf = run(Chain(lib, everything, 64, device, gen), reps=5)
+    out["linears_m64"] = {"ms_per_step": round(t, 3), "GBps": round(gbps, 1), "TFLOPs": round(tf, 1),
+                          "note": "the 196 linears of a batch-64 decode step (tensor-core path), no attention"}
+    return out
+
+
+def gemm_section(lib, layers, device, gen, tensor_peak: float) -> dict | None:
+    """The seven shapes at M = 2048 on the tensor-core kernel (4 layers each,
+    inputs 6-37 MB per launch), and q/k/v as one grouped call."""
+    gemm = {"m": 2048, "per_shape": {}}
+    total_flops, total_ms = 0, 0.0
+    for idx, (name, k, n, has_bias) in enumerate(SHAPES):
+        chain = Chain(lib, [layers[i][idx] for i in range(4)], 2048, device, gen, algo=2)
+        t = time_graph(chain.graph(), reps=10, warmup=3)
+        tf = chain.flops() / (t / 1e3) / 1e12
+        gemm["per_shape"][name] = {"TFLOPs": tf, "us_per_launch": t * 1e3 / 4, "frac_of_bf16_peak": tf / tensor_peak}
+        total_flops += chain.flops()
+        total_ms += t
+    gemm["TFLOPs_all_shapes"] = total_flops / (total_ms / 1e3) / 1e12
+    gemm["frac_of_bf16_peak"] = gemm["TFLOPs_all_shapes"] / tensor_peak
+    grouped = GroupedChain(lib, layers[:4], device, gen, m=2048)
+    grouped.launches = grouped.launches[0::4]  # the q/k/v group of each layer
+    t = time_graph(grouped.graph(), reps=10, warmup=3)
+    flops = 4 * 2 * 2048 * 1536 * (1536 + 256 + 256)
+    gemm["qkv_grouped"] = {"TFLOPs": flops / (t / 1e3) / 1e12, "us_per_launch": t * 1e3 / 4,
+                           "frac_of_bf16_peak": flops / (t / 1e3) / 1e12 / tensor_peak}
+    return gemm
+
+
+def e2e_section(pkg, step: DecodeStep, device, steps: int, dist) -> dict:
+    """The headline step through the public Python API with host buffers:
+    the API calls are captured once in a CUDA graph (as DecodeEngine does);
+    each timed step copies the 28 layers' activations from pinned host memory,
+    replays, and reads the 28 down_proj outputs back."""
+    n = len(step.layers)
+    x_dev = torch.empty(n, 1, 1536, device=device, dtype=torch.bfloat16)
+    x_host = torch.cat([L.x for L in step.layers]).view(n, 1, 1536).cpu().pin_memory()
+    mods = [{k: as_module(v) for k, v in L.by.items()} for L in step.layers]
+    outs = []
+
+    def api_step():
+        outs.clear()
+        for i, m in enumerate(mods):
+            q, _, _ = pkg.b200_w4g64_linear_multi(x_dev[i], [m["q"], m["k"], m["v"]])
+            o = pkg.b200_w4g64_linear(q, m["o"].qweight, m["o"].scales, m["o"].zeros, None, out_features=1536,
+                                      in_features=1536, group_size=64, packing="canonical")
+            h = pkg.b200_w4g64_gate_up_silu(o, m["gate"], m["up"])
+            outs.append(pkg.b200_w4g64_linear(h, m["down"].qweight, m["down"].scales, m["down"].zeros, None,
+                                              out_features=1536, in_features=8960, group_size=64,
+                                              packing="canonical"))
+
+    x_dev.copy_(x_host)
+    g = capture(api_step)  # `outs` now holds the graph's output tensors, rewritten by every replay
+    y_host = torch.empty((n, 1, 1536), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        g.replay()
+        y_host.copy_(torch.stack(outs), non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record()
+    for _ in range(steps):
+        e2e_step()
+    ee.record()
+    ee.synchronize()
+    ms = max_over_ranks(dist, es.elapsed_time(ee) / steps, device)
+    return {"ms_per_step": ms, "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 4,
+            "api": "b200_w4g64_linear_multi / b200_w4g64_linear / b200_w4g64_gate_up_silu per layer, captured "
+                   "once in a CUDA graph; pinned host copies in the timed region"}
+
+
+def serving_section(device, dist, world: int, full: bool) -> dict:
+    """The decode engine (engine.DecodeEngine) on the reference model with
+    random W4G64 weights: prompt through the reference model on the b200
+    backend, then graph-captured greedy steps. Config 4 (batch 64, 1024-token
+    prompts, 256 steps) on every rank as an independent replica; config 3
+    (batch 1, 512-token prompt, 128 steps) on one GPU. tok/s = batch x steps /
+    decode time (CUDA events, max over ranks)."""
     q2 = importlib.import_module(PACKAGE + ".qwen2")
     try:
         q2.reference_package()
+    except ImportError as exc:
+        return {"unavailable": f"reference package not installed: {exc}"}
+    eng_mod = importlib.import_module(PACKAGE + ".engine")
+    rank = dist.get_rank() if dist else 0
+    model = q2.build_random_qwen2(device=device, seed=0)
+    out = {"model": "Qwen2-1.5B random-init W4G64 RTN (reference model.py), engine.DecodeEngine",
+           "data": "uniform random prompt ids, seeded per rank"}
+    cases = (("config4", 64, 1024, 256),) if not full else (("config3", 1, 512, 128), ("config4", 64, 1024, 256))
+    for name, B, P, n in cases:
+        prompt = torch.randint(0, model.config.vocab_size, (B, P),
+                               generator=torch.Generator().manual_seed(31 + rank)).to(device)
+        eng = eng_mod.DecodeEngine(model, batch=B, max_len=P + n + 1)
+        eng.generate(prompt[:, :16], 4)  # capture + warm-up
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with ClockSampler(device.index) as clocks:
+            ev[0].record()
+            eng.prefill(prompt)
+            ev[1].record()
+            tokens = eng.decode(n)
+            ev[2].record()
+            ev[2].synchronize()
+        prefill_ms = max_over_ranks(dist, ev[0].elapsed_time(ev[1]), device)
+        decode_ms = max_over_ranks(dist, ev[1].elapsed_time(ev[2]), device)
+        out[name] = {"batch": B, "prompt_tokens": P, "new_tokens": n, "prefill_ms": prefill_ms,
+                     "decode_ms_per_step": decode_ms / n, "tok_s_per_gpu": B * n / (decode_ms / 1e3),
+                     "tok_s": world * B * n / (decode_ms / 1e3), "replicas": world,
+                     "distinct_tokens": int(tokens.unique().numel()), "clocks": clocks.summary()}
+        del eng
+        torch.cuda.empty_cache()
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
+def reference_harness_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
+    """Batch-1 decode through the reference's own ``greedy_generate_cached``
+    on the b200 backend (its attention code, then the b200 decode attention
+    patched in, ``fast_attention``), the torch backend for comparison (fewer
+    steps), and the final-logits cosine of the prompt forward: b200 against
+    the torch backend (FP32 dequantise-then-matmul)."""
+    q2 = importlib.import_module(PACKAGE + ".qwen2")
+    try:
+        ref = q2.reference_package()
     except ImportError as exc:
         return {"unavailable": f"reference package not installed: {exc}"}
     gen_mod = importlib.import_module("qwen_int4.generation")
@@ -368,37 +656,49 @@ def e2e_decode(device, prompt_len: int = 512, new_tokens: int = 128) -> dict:
         return a.elapsed_time(b), out
 
     result = {"model": "Qwen2-1.5B random-init W4G64 RTN (reference model.py)", "batch": 1,
-              "prompt_tokens": prompt_len,
-              "harness": "cuDNN SDPA backend disabled (per-call graph builds as the KV cache grows)"}
+              "prompt_tokens": prompt_len, "harness": "qwen_int4.generation.greedy_generate_cached"}
     cudnn_sdp = torch.backends.cuda.cudnn_sdp_enabled()
-    torch.backends.cuda.enable_cudnn_sdp(False)
-    with torch.inference_mode():
-        for leg, backend, fuse, steps in (("b200", "b200", False, new_tokens),
-                                          ("b200_fused_mlp", "b200", True, new_tokens),
-                                          ("torch", "torch", False, 8)):
-            q2.register_with_reference(q2.reference_package().__name__, fuse_mlp=fuse)
-            model.set_backend(backend)
-            gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=3)  # warm-up at full length
-            prefill_ms, _ = timed(lambda: model(prompt, use_cache=True))
-            total_ms, _ = timed(lambda: gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=steps))
-            decode_ms = max(total_ms - prefill_ms, 1e-6)
-            result[leg] = {"prefill_ms": prefill_ms, "new_tokens": steps,
-                               "generate_ms": total_ms, "decode_tok_s": steps / (decode_ms / 1e3)}
-    torch.backends.cuda.enable_cudnn_sdp(cudnn_sdp)
-    result["decode_tok_s"] = result["b200"]["decode_tok_s"]
-    result["decode_tok_s_fused_mlp"] = result["b200_fused_mlp"]["decode_tok_s"]
+    torch.backends.cuda.enable_cudnn_sdp(False)  # per-call graph builds as the KV cache grows
+    try:
+        with torch.inference_mode():
+            for leg, backend, fast, steps in (("b200", "b200", False, new_tokens),
+                                              ("b200_fast_attention", "b200", True, new_tokens),
+                                              ("torch", "torch", False, 8)):
+                q2.register_with_reference(ref.__name__, fast_attention=fast)
+                model.set_backend(backend)
+                gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=3)
+                prefill_ms, _ = timed(lambda: model(prompt, use_cache=True))
+                total_ms, _ = timed(lambda: gen_mod.greedy_generate_cached(model, prompt, max_new_tokens=steps))
+                decode_ms = max(total_ms - prefill_ms, 1e-6)
+                result[leg] = {"prefill_ms": prefill_ms, "new_tokens": steps, "generate_ms": total_ms,
+                               "decode_tok_s": steps / (decode_ms / 1e3)}
+            q2.register_with_reference(ref.__name__, fast_attention=False)
+            model.set_backend("b200")
+            lb = model(prompt).float()
+            model.set_backend("torch")
+            lt = model(prompt).float()
+        cos_last = torch.nn.functional.cosine_similarity(lb[0, -1], lt[0, -1], dim=0)
+        cos_all = torch.nn.functional.cosine_similarity(lb.flatten(), lt.flatten(), dim=0)
+        result["final_logits_cosine_vs_torch_backend"] = {"last_position": float(cos_last),
+                                                          "all_positions": float(cos_all)}
+    finally:
+        q2.register_with_reference(ref.__name__, fast_attention=False)
+        torch.backends.cuda.enable_cudnn_sdp(cudnn_sdp)
+    result["decode_tok_s"] = result["b200_fast_attention"]["decode_tok_s"]
     del model
     torch.cuda.empty_cache()
     return result
 
 
 def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> dict:
-    """Column-split prefill: one Qwen2-1.5B MLP (gate/up/down) at M tokens with
-    gate/up/down column-split over the ranks and NCCL all-gathers (two per
-    MLP). Time is the max over ranks of CUDA-event time per forward."""
+    """One Qwen2-1.5B MLP (gate/up/down) at M = 4096 tokens through
+    parallel.ColumnParallelMLP: unsplit on one GPU (N = 1, no collectives),
+    or split over the ranks in both modes (column: two all-gathers;
+    column_row: one all-reduce). Time is the max over ranks of CUDA-event
+    time per forward; every output is checked against the unsplit MLP
+    computed on the same rank."""
     par = importlib.import_module(PACKAGE + ".parallel")
-    from types import SimpleNamespace
-
+    pkg = importlib.import_module(PACKAGE)
     gen = torch.Generator(device=device).manual_seed(5)
 
     def qlinear(n, k):
@@ -406,65 +706,37 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
         return SimpleNamespace(qweight=qw, scales=sc, zeros=z, bias=None, in_features=k, out_features=n)
 
     mlp = SimpleNamespace(gate_proj=qlinear(8960, 1536), up_proj=qlinear(8960, 1536), down_proj=qlinear(1536, 8960))
-    split = par.ColumnParallelMLP(mlp)
     x = torch.randn(m, 1536, device=device, generator=gen).to(torch.bfloat16)
-    for _ in range(3):
-        split(x)
-    torch.cuda.synchronize()
-    dist.barrier()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        split(x)
-    b.record()
-    b.synchronize()
-    ms = torch.tensor([a.elapsed_time(b) / reps], device=device)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     flops = 2 * m * 1536 * 8960 * 3
-    return {"m": m, "ms_per_mlp": float(ms.item()), "TFLOPs": flops / (float(ms.item()) / 1e3) / 1e12,
-            "collectives": "2 x all_gather_into_tensor (NCCL) per MLP", "ranks": world}
-
-
-def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
-    """Secondary figures for the workloads the headline does not cover:
-    config 0 (gate, symmetric, M = 1/4/16), config 1's remaining M points
-    (8/32/128/512, seven shapes of four layers), config 2 (AWQ-style
-    asymmetric down_proj, M = 1/16/2048) and config 4's batch-64 decode step
-    (196 linears at M = 64). Library-chosen kernels (GEMV up to M = 16,
-    tensor cores above), CUDA graphs of C-ABI launches."""
-    q2 = importlib.import_module(PACKAGE + ".qwen2")
-    out = {}
-
-    def run(chain, reps=10):
-        t = time_graph(chain.graph(), reps=reps, warmup=3)
-        return t, chain.bytes() / (t / 1e3) / 1e9, chain.flops() / (t / 1e3) / 1e12
-
-    gates = [layer[4] for layer in layers]
-    out["cfg0_gate_sym_GBps"] = {f"m{m}": round(run(Chain(lib, gates, m, device, gen))[1], 1) for m in (1, 4, 16)}
-    sweep = {}
-    for m in (8, 32, 128, 512):
-        t, gbps, tf = run(Chain(lib, [e for layer in layers[:4] for e in layer], m, device, gen))
-        sweep[f"m{m}"] = {"GBps": round(gbps, 1), "TFLOPs": round(tf, 2), "ms_4_layers": round(t, 4)}
-    out["cfg1_seven_shapes"] = sweep
-    # Config 2: per-input-channel scaled weights, asymmetric RTN, activations divided by the channel scale.
-    chan = torch.exp(torch.empty(8960, device=device).uniform_(float(np.log(0.5)), float(np.log(2.0)), generator=gen))
-    downs = []
-    for _ in range(4):
-        w = torch.randn(1536, 8960, device=device, generator=gen) * 0.02 * chan
-        qw, sc, z = q2.quantize_asymmetric_rtn_torch(w.to(torch.bfloat16).float())
-        downs.append({"name": "down_awq", "k": 8960, "n": 1536, "qweight": qw, "scales": sc, "zeros": z, "bias": None})
-    cfg2 = {}
-    for m in (1, 16, 2048):
-        chain = Chain(lib, downs, m, device, gen)
-        chain.x = [(x.float() / chan).to(torch.bfloat16) for x in chain.x]
-        t, _, tf = run(chain)
-        nbytes = sum(alg_bytes(m, 1536, 8960, False, asym=True) for _ in downs)
-        cfg2[f"m{m}"] = {"GBps": round(nbytes / (t / 1e3) / 1e9, 1)} if m <= 16 else \
-            {"TFLOPs": round(tf, 1), "frac_of_bf16_peak": round(tf / tensor_peak, 3)}
-    out["cfg2_awq_down"] = cfg2
-    t, _, tf = run(Chain(lib, [e for layer in layers for e in layer], 64, device, gen), reps=5)
-    out["cfg4_decode_m64"] = {"ms_per_step": round(t, 3), "tokens_per_s": round(64 / (t / 1e3), 1),
-                              "TFLOPs": round(tf, 1), "note": "196 linears at M = 64 (tensor-core path), one GPU"}
+    d = mlp.down_proj
+    ref = pkg.b200_w4g64_linear(pkg.b200_w4g64_gate_up_silu(x, mlp.gate_proj, mlp.up_proj), d.qweight, d.scales,
+                                d.zeros, None, out_features=1536, in_features=8960, group_size=64,
+                                packing="canonical").to(torch.bfloat16).float()
+    out = {"m": m, "ranks": world}
+    for mode in (("column",) if world == 1 else par.ColumnParallelMLP.MODES):
+        split = par.ColumnParallelMLP(mlp, mode=mode)
+        for _ in range(3):
+            y = split(x)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            split(x)
+        b.record()
+        b.synchronize()
+        ms = max_over_ranks(dist, a.elapsed_time(b) / reps, device)
+        yf = y.float()
+        cos = float(torch.nn.functional.cosine_similarity(yf.flatten(), ref.flatten(), dim=0))
+        err = float((yf - ref).abs().max())
+        key = "unsplit" if world == 1 else mode
+        out[key] = {"ms_per_mlp": ms, "TFLOPs": flops / (ms / 1e3) / 1e12,
+                    "check_vs_unsplit": {"cosine": cos, "max_abs_err": err,
+                                         "ok": bool(cos > 0.99999 and err <= 2e-2 + 2 ** -7 * float(ref.abs().max()))},
+                    "collectives": {"column": "2 x all_gather_into_tensor (FP32 intermediate, bf16 output)",
+                                    "column_row": "1 x all_reduce (FP32 output partial sums)"}.get(mode)
+                    if world > 1 else "none (one GPU)"}
     return out
 
 
@@ -500,9 +772,11 @@ def main() -> None:
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm", action="store_true")
-    parser.add_argument("--no-model", action="store_true", help="skip the Qwen2-1.5B decode tok/s section")
+    parser.add_argument("--no-model", action="store_true",
+                        help="skip the model sections (serving engine, reference harness decode)")
     parser.add_argument("--no-configs", action="store_true",
-                        help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, AWQ down, batch-64 linears)")
+                        help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, "
+                             "AWQ down, batch-64 linears)")
     parser.add_argument("--profile-case", choices=["gemv", "gemm"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
                              "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv) or M=2048 (gemm)")
@@ -527,18 +801,14 @@ def main() -> None:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=device)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
 
     pkg = importlib.import_module(PACKAGE)
     lib = importlib.import_module(PACKAGE + "._lib").load()
     layers = build_model_weights(device, seed=1234 + rank)
     gen = torch.Generator(device=device).manual_seed(99 + rank)
-    entries = [e for layer in layers for e in layer]
-    step_chain = Chain(lib, entries, 1, device, gen)
-    step_graph = step_chain.graph()
-    step_bytes = step_chain.bytes()
-    launches_per_step = len(entries)
+    step = DecodeStep(lib, layers, device, gen)
+    step_graph = step.graph()
 
     # Timed region: K replays of the step graph, barrier + sync on both sides.
     for _ in range(args.warmup):
@@ -557,30 +827,19 @@ def main() -> None:
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    ms = start.elapsed_time(end)
-    if dist:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(dist, start.elapsed_time(end), device)
     ms_per_step = ms / args.steps
-    value = step_bytes * world * args.steps / (ms / 1e3) / 1e9
+    value = step.nbytes * world * args.steps / (ms / 1e3) / 1e9
 
     # Dominant kernel: the gate GEMV at M=1, chained over the 28 layers.
     per_shape = {}
     for idx, (name, k, n, has_bias) in enumerate(SHAPES):
         chain = Chain(lib, [layer[idx] for layer in layers], 1, device, gen)
-        g = chain.graph()
-        t = time_graph(g, reps=20, warmup=3)
-        per_shape[name] = {"m": 1, "us_per_launch": t * 1e3 / LAYERS,
-                           "GBps": chain.bytes() / (t / 1e3) / 1e9}
+        t = time_graph(chain.graph(), reps=20, warmup=3)
+        per_shape[name] = {"m": 1, "us_per_launch": t * 1e3 / LAYERS, "GBps": chain.bytes() / (t / 1e3) / 1e9}
     gate = per_shape["gate"]
+    variants = step_variants(lib, layers, device, gen, dist)
 
-    # The same step with the input-sharing linears grouped per launch.
-    grouped = GroupedChain(lib, layers, device, gen)
-    t = time_graph(grouped.graph(), reps=20, warmup=3)
-    decode_grouped = {"launches_per_step": len(grouped.launches), "ms_per_step": t,
-                      "GBps": step_bytes / (t / 1e3) / 1e9,
-                      "api": "qi4_w4g64_linear_multi (q/k/v and gate/up grouped), CUDA graph"}
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     if peaks_path.exists():
         peaks = json.loads(peaks_path.read_text())
@@ -592,76 +851,26 @@ def main() -> None:
     roofline = {"bound": "hbm", "kernel": "gemv_mma_kernel (gate 1536->8960, M=1)",
                 "achieved": gate["GBps"], "peak": hbm_peak, "unit": "GB/s",
                 "frac": gate["GBps"] / hbm_peak, "peak_source": peak_src,
-                "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False)}
+                "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False),
+                "step_frac": step.nbytes / (ms_per_step / 1e3) / 1e9 / hbm_peak}
 
-    configs = None
-    if not args.no_configs and world == 1:
-        configs = config_sweep(lib, layers, device, gen, tensor_peak)
+    configs = config_sweep(lib, layers, device, gen, tensor_peak) if not args.no_configs and world == 1 else None
+    gemm = gemm_section(lib, layers, device, gen, tensor_peak) if not args.no_gemm and world == 1 else None
 
-    # GEMM at M=2048 (tensor-core kernel) over one layer's seven shapes.
-    gemm = None
-    if not args.no_gemm and world == 1:
-        gemm = {"m": 2048, "per_shape": {}}
-        total_flops, total_ms = 0, 0.0
-        for idx, (name, k, n, has_bias) in enumerate(SHAPES):
-            chain = Chain(lib, [layers[i][idx] for i in range(4)], 2048, device, gen, algo=2)
-            try:
-                g = chain.graph()
-            except RuntimeError:
-                gemm = None
-                break
-            t = time_graph(g, reps=10, warmup=3)
-            tf = chain.flops() / (t / 1e3) / 1e12
-            gemm["per_shape"][name] = {"TFLOPs": tf, "us_per_launch": t * 1e3 / 4}
-            total_flops += chain.flops()
-            total_ms += t
-        if gemm is not None:
-            gemm["TFLOPs_all_shapes"] = total_flops / (total_ms / 1e3) / 1e12
-            gemm["frac_of_bf16_peak"] = gemm["TFLOPs_all_shapes"] / tensor_peak
+    e2e_steps = max(3, min(args.steps, 50))
+    e2e = e2e_section(pkg, step, device, e2e_steps, dist)
+    e2e = {"value": step.nbytes * world / (e2e["ms_per_step"] / 1e3) / 1e9, "unit": UNIT, **e2e}
 
-    # End to end through the public API with host buffers.
-    x_host = torch.cat([x.view(-1) for x in step_chain.x]).cpu().pin_memory()
-    out_host = torch.empty(sum(e["n"] for e in entries), dtype=torch.bfloat16).pin_memory()
-    offsets, off = [], 0
-    for e in entries:
-        offsets.append(off)
-        off += e["k"]
+    split = split_prefill(device, dist, world)
 
-    def e2e_step():
-        xd = x_host.to(device, non_blocking=True)
-        outs = []
-        for e, o in zip(entries, offsets):
-            outs.append(pkg.b200_w4g64_linear(
-                xd[o:o + e["k"]].view(1, e["k"]), e["qweight"], e["scales"], e["zeros"], e["bias"],
-                out_features=e["n"], in_features=e["k"], group_size=64, packing="canonical"))
-        out_host.copy_(torch.cat([t.view(-1) for t in outs]), non_blocking=True)
-
-    e2e_steps = max(3, min(args.steps, 20))
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    es.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    ee.record()
-    ee.synchronize()
-    e2e_ms = es.elapsed_time(ee) / e2e_steps
-    if dist:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = {"value": step_bytes * world / (e2e_ms / 1e3) / 1e9, "unit": UNIT,
-           "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
-           "ms_per_step": e2e_ms, "api": "b200_w4g64_linear per linear (Python call; C++ binding of the C ABI)"}
-
-    split = split_prefill(device, dist, world) if dist else None
-
-    decode = None
-    if not args.no_model and world == 1:
-        del layers, entries, step_chain, step_graph
-        torch.cuda.empty_cache()
-        decode = e2e_decode(device)
+    step_bytes = step.nbytes
+    del layers, step, step_graph
+    torch.cuda.empty_cache()
+    serving = decode = None
+    if not args.no_model:
+        serving = serving_section(device, dist, world, full=world == 1)
+        if world == 1:
+            decode = reference_harness_decode(device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -676,14 +885,14 @@ def main() -> None:
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init W4G64 RTN weights)",
-        "config": {"workload": WORKLOAD, "m": 1, "layers": LAYERS, "linears_per_step": launches_per_step,
-                   "bytes_per_step": step_bytes, "parallelism": f"replicas x{world}",
+        "config": {"workload": WORKLOAD, "m": 1, "layers": LAYERS, "launches_per_step": 4 * LAYERS,
+                   "bytes_per_step": step_bytes,
+                   "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
-        "gpu_launches": launches_per_step * args.steps,
-        "roofline": roofline, "per_shape_m1": per_shape, "decode_step_grouped": decode_grouped,
-        "gemm_m2048": gemm, "configs": configs, "qwen2_decode": decode,
-        "split_prefill_mlp": split,
-        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
+        "gpu_launches": 4 * LAYERS * args.steps,
+        "roofline": roofline, "per_shape_m1": per_shape, "decode_step_variants": variants,
+        "gemm_m2048": gemm, "configs": configs, "serving": serving, "qwen2_decode": decode,
+        "split_prefill_mlp": split, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))
 
 

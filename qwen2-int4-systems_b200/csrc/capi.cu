@@ -261,19 +261,15 @@ static int linear_multi_impl(const void* x, int x_dtype, int64_t M, int64_t K, i
     if (rc) return rc;
   }
   if (!any_bias) bias_dtype = QI4_DTYPE_NONE;
-  if (M > kGemvMaxM) {
-    // Prefill sizes: one tensor-core launch per matrix.
-    for (int i = 0; i < count; ++i) {
-      const int rc = linear_impl(x, x_dtype, M, K, qweights[i], scales[i], zeros ? zeros[i] : nullptr,
-                                 biases ? biases[i] : nullptr, bias_dtype, outs[i], Ns[i], stream_ptr,
-                                 QI4_ALGO_AUTO, 1);
-      if (rc) return rc;
-    }
-    return QI4_OK;
-  }
   DeviceInfo info;
   int rc = current_device(info);
   if (rc) return rc;
+  if (M > kGemvMaxM) {
+    // Prefill sizes: one tensor-core launch over the tiles of every matrix.
+    return check_launch(launch_gemm_tc_multi(x, x_dtype, M, K, count, qweights, scales, zeros, biases, bias_dtype,
+                                             outs, Ns, static_cast<cudaStream_t>(stream_ptr), true, info.sms),
+                        "w4g64 grouped tensor-core GEMM");
+  }
   const uint8_t* zs[3] = {nullptr, nullptr, nullptr};
   const void* bs[3] = {nullptr, nullptr, nullptr};
   int64_t n_eff = 0;
@@ -319,9 +315,9 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
     return check_launch(launch_gemv_swiglu(x, x_dtype, M, K, qws, scs, zs, out, N, stream, true, plan),
                         "w4g64 fused gate/up SwiGLU GEMV");
   }
-  // Prefill sizes: both projections on the tensor cores into scratch (their
-  // outputs in the activation dtype, as QuantLinear returns them), then the
-  // elementwise SwiGLU.
+  // Prefill sizes: both projections in one tensor-core launch into scratch
+  // (their outputs in the activation dtype, as QuantLinear returns them),
+  // then the elementwise SwiGLU.
   const size_t xsize = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
   const size_t bytes = (size_t)M * (size_t)N * xsize;
   const size_t half = (bytes + 255) / 256 * 256;
@@ -332,10 +328,11 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
   }
   void* g = scratch;
   void* u = static_cast<char*>(scratch) + half;
-  rc = linear_impl(x, x_dtype, M, K, qw_gate, sc_gate, z_gate, nullptr, QI4_DTYPE_NONE, g, N, stream_ptr,
-                   QI4_ALGO_AUTO, 1);
-  if (!rc)
-    rc = linear_impl(x, x_dtype, M, K, qw_up, sc_up, z_up, nullptr, QI4_DTYPE_NONE, u, N, stream_ptr, QI4_ALGO_AUTO, 1);
+  void* outs[2] = {g, u};
+  const int64_t Ns[2] = {N, N};
+  rc = check_launch(launch_gemm_tc_multi(x, x_dtype, M, K, 2, qws, scs, zs, nullptr, QI4_DTYPE_NONE, outs, Ns, stream,
+                                         true, info.sms),
+                    "w4g64 gate/up tensor-core GEMM");
   if (!rc) rc = check_launch(launch_swiglu_elementwise(g, u, x_dtype, out, M * N, stream, info.sms), "SwiGLU");
   scratch_free(scratch, stream);
   return rc;

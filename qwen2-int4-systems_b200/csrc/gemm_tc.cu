@@ -48,10 +48,23 @@ __device__ int g_gemm_tc_error;
 namespace {
 
 // A (dequantised, in TMEM) + B (activations, in shared memory) stages in
-// flight. Measured on B200 at M = 2048 over the seven Qwen2 shapes: 3 stages
-// 700 TFLOP/s aggregate, 4 stages 734, 5 stages 717.
-constexpr int kStages = 4;
-constexpr int kPStages = 2;     // packed-weight boxes (4 groups each)
+// flight, by the activation tile's width (x_tiles = 2 for FP32 activations,
+// carried as bf16 hi + lo). Measured on B200 at M = 2048 over the seven Qwen2
+// shapes with 256-token tiles: 3 stages 700 TFLOP/s aggregate, 4 stages 734,
+// 5 stages 717. Narrow tiles compute little per stage, so the round trip
+// dequantise -> MMA -> commit -> dequantise the next use of the slot bounds
+// them; they take more slots (the TMEM columns and shared memory are there:
+// 64 + 12 x 32 columns at 64 tokens).
+__host__ __device__ constexpr int a_stages(int x_tiles, int bn) {
+  return x_tiles * bn <= 64 ? 12 : x_tiles * bn <= 128 ? 6 : 4;
+}
+// Packed-weight boxes (4 groups, 16 KB each) in flight: what shared memory
+// leaves beside the activation stages (and the K split's partial tile). At
+// least ~45 KB per SM covers the HBM latency (Little's law: ~1 us x the SM's
+// share of the bandwidth); wide tiles compute long enough per box for two.
+__host__ __device__ constexpr int p_stages(int x_tiles, int bn) {
+  return x_tiles * bn <= 64 ? 5 : x_tiles * bn <= 128 ? 3 : x_tiles * bn <= 192 ? 4 : 2;
+}
 constexpr int kTileN = 128;     // weight rows per tile (UMMA M)
 // Dequantise/epilogue warps per CTA: 16 (one CTA per SM, tiles up to 256
 // tokens) or 8 (128-token tiles, two CTAs per SM, so that one CTA's prologue
@@ -59,28 +72,45 @@ constexpr int kTileN = 128;     // weight rows per tile (UMMA M)
 // plus these.
 __host__ __device__ constexpr int gemm_threads(int dw) { return 64 + 32 * dw; }
 
-// Tensor-memory columns: the FP32 accumulator (BN) plus kStages A stages of 32
+// Tensor-memory columns: the FP32 accumulator (BN) plus the A stages of 32
 // columns (64 bf16 K elements of 128 rows), rounded up to a power of two.
-__host__ __device__ constexpr uint32_t tmem_cols(int bn) {
-  return bn + 32 * kStages <= 128 ? 128u : (bn + 32 * kStages <= 256 ? 256u : 512u);
+__host__ __device__ constexpr uint32_t tmem_cols(int bn, int stages) {
+  return bn + 32 * stages <= 128 ? 128u : (bn + 32 * stages <= 256 ? 256u : 512u);
 }
 constexpr int kABytes = kTileN * 128;   // one group of 128 rows in bf16: 16 KB
 constexpr int kPBytes = kTileN * 128;   // one packed box: 128 rows x 128 B
 
-struct Args {
-  int M;
-  int64_t N, K;
+constexpr int kMaxMats = 3;  // weight matrices sharing the activations in one launch (q/k/v, gate/up)
+
+// One weight matrix of a launch.
+struct Mat {
+  int64_t N;
   const __half* scales;
   const uint8_t* zeros;
   const void* bias;
-  int bias_dtype;
   void* out;
+};
+
+struct Args {
+  int M;
+  int64_t K;
+  Mat mat[kMaxMats];
+  int tiles_end[kMaxMats];  // cumulative 128-row tiles: matrix m owns tiles [tiles_end[m-1], tiles_end[m])
+  int nmats;
+  int bias_dtype;
   int out_dtype;
   int BN;
   int tma_out;  // 1: output tile staged in shared memory and written by one TMA store
   int dw;       // dequantise/epilogue warps per CTA (16; the kernel also compiles for 8)
   int ksplit;   // CTAs per cluster along K (grid z); > 1 reduces FP32 partial tiles over DSMEM
   int bps;      // packed 128-byte boxes (4 groups) per K split
+};
+
+// The tensor maps of a launch: packed weights and outputs per matrix, activations (and their lo half).
+struct Maps {
+  CUtensorMap w[kMaxMats];
+  CUtensorMap x, x_lo;
+  CUtensorMap o[kMaxMats];
 };
 
 // ---- tcgen05 wrappers ------------------------------------------------------
@@ -201,8 +231,10 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t word, float s16, float nz
 
 template <int XT, int BN, int DW>
 __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                   const __grid_constant__ CUtensorMap xmap_lo, const __grid_constant__ CUtensorMap omap,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
+                   const __grid_constant__ CUtensorMap wmap2, const __grid_constant__ CUtensorMap xmap,
+                   const __grid_constant__ CUtensorMap xmap_lo, const __grid_constant__ CUtensorMap omap0,
+                   const __grid_constant__ CUtensorMap omap1, const __grid_constant__ CUtensorMap omap2,
                    const Args a) {
   extern __shared__ uint8_t smem_raw[];
   // Offset from the shared array itself (not an integer round trip), so that
@@ -211,7 +243,10 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
   // FP32 activations arrive as two bf16 tiles (x = hi + lo), loaded together.
   constexpr int kXTiles = XT == QI4_DTYPE_F32 ? 2 : 1;
   constexpr int kBBytes = kXTiles * BN * 128;       // BN rows x 64 elements (2 bytes), per tile
-  constexpr uint32_t kTmemCols = tmem_cols(BN);     // D (BN columns) + A stages (32 columns each)
+  constexpr int kStages = a_stages(kXTiles, BN);
+  constexpr int kPStages = p_stages(kXTiles, BN);
+  constexpr uint32_t kTmemCols = tmem_cols(BN, kStages);  // D (BN columns) + A stages (32 columns each)
+  static_assert(BN + 32 * kStages <= 512, "accumulator and A stages must fit tensor memory");
   uint8_t* sB = smem;                               // kStages x BN*128
   uint8_t* sP = sB + kStages * kBBytes;             // kPStages x 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPStages * kPBytes);
@@ -226,7 +261,14 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
   float* part = reinterpret_cast<float*>(tmem_slot + 4);  // [BN][128] FP32 partial tile (K split only)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t n0 = (int64_t)blockIdx.x * kTileN;
+  // This CTA's matrix and its 128-row tile within that matrix.
+  const int tile = blockIdx.x;
+  const int mi = (a.nmats > 1 && tile >= a.tiles_end[0]) + (a.nmats > 2 && tile >= a.tiles_end[1]);
+  const Mat& mt = mi == 0 ? a.mat[0] : (mi == 1 ? a.mat[1] : a.mat[2]);
+  const CUtensorMap* wmap = mi == 0 ? &wmap0 : (mi == 1 ? &wmap1 : &wmap2);
+  const CUtensorMap* omap = mi == 0 ? &omap0 : (mi == 1 ? &omap1 : &omap2);
+  const int64_t N = mt.N;
+  const int64_t n0 = (int64_t)(tile - (mi == 0 ? 0 : a.tiles_end[mi - 1])) * kTileN;
   const int m0 = blockIdx.y * BN;
   // This CTA's K range: boxes [box0, box0 + bps) of the row (4 groups each).
   const int KT_all = (int)(a.K / kGroup);
@@ -258,7 +300,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      prefetch_tensor_map(&wmap);
+      prefetch_tensor_map(wmap);
       prefetch_tensor_map(&xmap);
       if constexpr (kXTiles == 2) prefetch_tensor_map(&xmap_lo);
       const int nbox = (KT + 3) / 4;
@@ -266,7 +308,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
       int pbox = 0;
       for (; pbox < kPStages && pbox < nbox; ++pbox) {
         mbar_arrive_expect_tx(&p_full[pbox], kPBytes);
-        tma_load_2d(sP + pbox * kPBytes, &wmap, (box0 + pbox) * 128, (int)n0, &p_full[pbox]);
+        tma_load_2d(sP + pbox * kPBytes, wmap, (box0 + pbox) * 128, (int)n0, &p_full[pbox]);
       }
       pdl_wait();
       for (int k = 0; k < KT; ++k) {
@@ -282,7 +324,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
           const uint32_t pph = (uint32_t)(pbox / kPStages) & 1u;
           mbar_wait(&p_empty[p], pph ^ 1u, &g_gemm_tc_error);
           mbar_arrive_expect_tx(&p_full[p], kPBytes);
-          tma_load_2d(sP + p * kPBytes, &wmap, (box0 + pbox) * 128, (int)n0, &p_full[p]);
+          tma_load_2d(sP + p * kPBytes, wmap, (box0 + pbox) * 128, (int)n0, &p_full[p]);
           ++pbox;
         }
       }
@@ -321,9 +363,9 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     const int sub = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // tile row 0..127
     const int64_t row = n0 + r;
-    const bool row_ok = row < a.N;
+    const bool row_ok = row < N;
     const int64_t G = a.K / kGroup;
-    const __half* srow = a.scales + (row_ok ? row : 0) * G + kb;
+    const __half* srow = mt.scales + (row_ok ? row : 0) * G + kb;
     const int64_t zrow = (row_ok ? row : 0) * G + kb;
     const uint32_t sP_addr = smem_addr(sP);
     const uint32_t t_lane = (uint32_t)(quarter * 32) << 16;
@@ -334,7 +376,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       sc4[j] = (row_ok && j < KT) ? __half2float(__ldg(srow + j)) : 0.f;
-      z4[j] = (row_ok && j < KT) ? load_zero(a.zeros, zrow + j) : 0;
+      z4[j] = (row_ok && j < KT) ? load_zero(mt.zeros, zrow + j) : 0;
     }
     for (int pb = 0; pb < nbox; ++pb) {
       const int p = pb % kPStages;
@@ -343,7 +385,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
       for (int j = 0; j < 4; ++j) {
         const int kn = (pb + 1) * 4 + j;
         nsc4[j] = (row_ok && kn < KT) ? __half2float(__ldg(srow + kn)) : 0.f;
-        nz4[j] = (row_ok && kn < KT) ? load_zero(a.zeros, zrow + kn) : 0;
+        nz4[j] = (row_ok && kn < KT) ? load_zero(mt.zeros, zrow + kn) : 0;
       }
       mbar_wait(&p_full[p], pph, &g_gemm_tc_error);
       uint4 q[4];
@@ -396,7 +438,7 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
     constexpr int kSlices = DW / 4;  // warps per lane quarter; warp `sub` takes 32-column blocks sub, sub + kSlices, ...
     const int er = quarter * 32 + lane;                            // tile row of this thread
     const int64_t orow = n0 + er;
-    const float bv = (orow < a.N && a.bias) ? load_as_f32(a.bias, a.bias_dtype, orow) : 0.f;
+    const float bv = (orow < N && mt.bias) ? load_as_f32(mt.bias, a.bias_dtype, orow) : 0.f;
     // Output: each warp stages its 32 rows x 32 tokens of a column block as a
     // contiguous [32 tokens][32 rows] box in the activation ring (which the
     // finished main loop no longer uses) and stores it with its own TMA store
@@ -426,13 +468,13 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
         fence_proxy_async_smem();  // this thread's staged values -> visible to the TMA engine
         __syncwarp();
         // (a box wholly past the last row or token is not issued; partial boxes are clipped by the TMA)
-        if (lane == 0 && n0 + quarter * 32 < a.N && m0 + c0 < a.M)
-          tma_store_2d(&omap, (int)n0 + quarter * 32, m0 + c0, box);
-      } else if (orow < a.N) {
+        if (lane == 0 && n0 + quarter * 32 < N && m0 + c0 < a.M)
+          tma_store_2d(omap, (int)n0 + quarter * 32, m0 + c0, box);
+      } else if (orow < N) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int m = m0 + c0 + j;
-          if (m < a.M) store_from_f32(a.out, a.out_dtype, (int64_t)m * a.N + orow, __uint_as_float(v[j]) + bv);
+          if (m < a.M) store_from_f32(mt.out, a.out_dtype, (int64_t)m * N + orow, __uint_as_float(v[j]) + bv);
         }
       }
     }
@@ -456,9 +498,9 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
         for (int q = 0; q < nranks; ++q) sum += cluster.map_shared_rank(part, q)[c * kTileN + r];
         const int m = m0 + c;
         const int64_t n = n0 + r;
-        if (m < a.M && n < a.N) {
-          const float b = a.bias ? load_as_f32(a.bias, a.bias_dtype, n) : 0.f;
-          store_from_f32(a.out, a.out_dtype, (int64_t)m * a.N + n, sum + b);
+        if (m < a.M && n < N) {
+          const float b = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, n) : 0.f;
+          store_from_f32(mt.out, a.out_dtype, (int64_t)m * N + n, sum + b);
         }
       }
     }
@@ -475,14 +517,14 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
 }
 
 size_t smem_bytes(int BN, int x_tiles, int ksplit) {
-  return 1024 + (size_t)kStages * x_tiles * BN * 128 + (size_t)kPStages * kPBytes +
-         (3 * kStages + 2 * kPStages + 1) * sizeof(uint64_t) + 16 +
+  const int ps = p_stages(x_tiles, BN), st = a_stages(x_tiles, BN);
+  return 1024 + (size_t)st * x_tiles * BN * 128 + (size_t)ps * kPBytes +
+         (3 * st + 2 * ps + 1) * sizeof(uint64_t) + 16 +
          (ksplit > 1 ? (size_t)BN * kTileN * sizeof(float) : 0);
 }
 
 template <int XT, int BN, int DW>
-cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
-                      const CUtensorMap& omap, const Args& a, cudaStream_t stream, bool pdl) {
+cudaError_t launch_bn(const Maps& mp, const Args& a, cudaStream_t stream, bool pdl) {
   const size_t smem = smem_bytes(BN, XT == QI4_DTYPE_F32 ? 2 : 1, a.ksplit);
   auto kernel = gemm_tc_kernel<XT, BN, DW>;
   static unsigned long long configured = 0;
@@ -497,7 +539,7 @@ cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CU
     configured |= bit;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.N + kTileN - 1) / kTileN), (unsigned)((a.M + BN - 1) / BN), (unsigned)a.ksplit);
+  cfg.gridDim = dim3((unsigned)a.tiles_end[a.nmats - 1], (unsigned)((a.M + BN - 1) / BN), (unsigned)a.ksplit);
   cfg.blockDim = dim3(gemm_threads(DW), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -517,22 +559,21 @@ cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& xmap, const CU
   }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, xmap_lo, omap, a);
+  return cudaLaunchKernelEx(&cfg, kernel, mp.w[0], mp.w[1], mp.w[2], mp.x, mp.x_lo, mp.o[0], mp.o[1], mp.o[2], a);
 }
 
 template <int XT>
-cudaError_t launch_x(const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
-                     const CUtensorMap& omap, const Args& a, cudaStream_t s, bool pdl) {
+cudaError_t launch_x(const Maps& mp, const Args& a, cudaStream_t s, bool pdl) {
   switch (a.BN) {
-    case 32: return launch_bn<XT, 32, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
-    case 64: return launch_bn<XT, 64, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
-    case 128: return launch_bn<XT, 128, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+    case 32: return launch_bn<XT, 32, 16>(mp, a, s, pdl);
+    case 64: return launch_bn<XT, 64, 16>(mp, a, s, pdl);
+    case 128: return launch_bn<XT, 128, 16>(mp, a, s, pdl);
     default:
       if constexpr (XT == QI4_DTYPE_F32) {
         return cudaErrorInvalidValue;  // FP32 tiles are <= 128 wide
       } else {
-        if (a.BN == 192) return launch_bn<XT, 192, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
-        return launch_bn<XT, 256, 16>(wmap, xmap, xmap_lo, omap, a, s, pdl);
+        if (a.BN == 192) return launch_bn<XT, 192, 16>(mp, a, s, pdl);
+        return launch_bn<XT, 256, 16>(mp, a, s, pdl);
       }
   }
 }
@@ -565,7 +606,7 @@ double plan_cost(int64_t M, int64_t N, int nbox, int bn, int ks, int num_sms) {
 // kernels do not pack every SM).
 void plan_tiles(Args& a, int x_dtype, int num_sms) {
   const int nbox = (int)((a.K / kGroup + 3) / 4);
-  const int64_t ntiles = (a.N + kTileN - 1) / kTileN;
+  const int64_t ntiles = a.tiles_end[a.nmats - 1];
   double best = 1e30;
   a.BN = 64;
   int ks_best = 1;
@@ -577,7 +618,7 @@ void plan_tiles(Args& a, int x_dtype, int num_sms) {
       if (kse > 1 && (bn > 128 || a.M > 512 ||
                       (double)(ntiles * ((a.M + bn - 1) / bn) * kse) > 0.65 * num_sms))
         continue;
-      const double t = plan_cost(a.M, a.N, nbox, bn, ks, num_sms);
+      const double t = plan_cost(a.M, ntiles * kTileN, nbox, bn, ks, num_sms);
       if (t < best) {
         best = t;
         a.BN = bn;
@@ -612,6 +653,50 @@ __global__ void __launch_bounds__(256) split_f32_kernel(const float4* __restrict
   }
 }
 
+// Fills the per-matrix part of `a` and the weight / output tensor maps; false
+// if a tensor map cannot describe a buffer. The output is written by TMA
+// stores when every matrix's row pitch allows it (a multiple of 16 bytes,
+// 16-byte-aligned base), else by direct stores.
+bool set_mats(Args& a, Maps& mp, int count, const uint8_t* const* qweights, const uint16_t* const* scales,
+              const uint8_t* const* zeros, const void* const* biases, void* const* outs, const int64_t* Ns) {
+  if (count < 1 || count > kMaxMats) return false;
+  int64_t tiles = 0;
+  bool tma_ok = true;
+  const int osz = a.out_dtype == QI4_DTYPE_F32 ? 4 : 2;
+  for (int i = 0; i < kMaxMats; ++i) {
+    const int j = i < count ? i : count - 1;  // unused slots repeat the last matrix
+    if (i < count) {
+      if (!tensor_map_2d(&mp.w[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(a.K / 2), (uint64_t)Ns[i],
+                         (uint64_t)(a.K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return false;
+      tiles += (Ns[i] + kTileN - 1) / kTileN;
+      tma_ok = tma_ok && (Ns[i] * osz) % 16 == 0 && reinterpret_cast<uintptr_t>(outs[i]) % 16 == 0;
+    } else {
+      mp.w[i] = mp.w[j];
+    }
+    a.mat[i].N = Ns[j];
+    a.mat[i].scales = reinterpret_cast<const __half*>(scales[j]);
+    a.mat[i].zeros = zeros ? zeros[j] : nullptr;
+    a.mat[i].bias = biases ? biases[j] : nullptr;
+    a.mat[i].out = outs[j];
+    if (tiles > (1 << 30)) return false;
+    a.tiles_end[i] = (int)tiles;
+  }
+  a.nmats = count;
+  a.tma_out = 0;
+  if (tma_ok) {
+    const CUtensorMapDataType ot = a.out_dtype == QI4_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : a.out_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    a.tma_out = 1;
+    for (int i = 0; i < count && a.tma_out; ++i)
+      a.tma_out = tensor_map_2d(&mp.o[i], outs[i], ot, (uint64_t)Ns[i], (uint64_t)a.M, (uint64_t)Ns[i] * osz, 32, 32,
+                                CU_TENSOR_MAP_SWIZZLE_NONE);
+    for (int i = count; i < kMaxMats; ++i) mp.o[i] = mp.o[count - 1];
+  }
+  return true;
+}
+
 }  // namespace
 
 void set_gemm_tc_override(int bn, int ksplit) {
@@ -625,29 +710,23 @@ bool tc_supported(int64_t M, int64_t N, int64_t K, int x_dtype) {
          (x_dtype == QI4_DTYPE_BF16 || x_dtype == QI4_DTYPE_F16 || x_dtype == QI4_DTYPE_F32);
 }
 
-cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
-                           const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
-                           int64_t N, cudaStream_t stream, bool pdl, int num_sms) {
-  Args a;
+cudaError_t launch_gemm_tc_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                                 const uint8_t* const* qweights, const uint16_t* const* scales,
+                                 const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                 void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl, int num_sms) {
+  Args a{};
+  Maps mp;
+  memset(&mp, 0, sizeof(mp));
   a.M = (int)M;
-  a.N = N;
   a.K = K;
-  a.scales = reinterpret_cast<const __half*>(scales);
-  a.zeros = zeros;
-  a.bias = bias;
   a.bias_dtype = bias_dtype;
-  a.out = out;
   a.out_dtype = x_dtype;
+  if (!set_mats(a, mp, count, qweights, scales, zeros, biases, outs, Ns)) return cudaErrorInvalidValue;
   plan_tiles(a, x_dtype, num_sms);
+  if (a.ksplit > 1) a.tma_out = 0;  // split tiles are finished by direct stores after the cluster reduction
   // 16 dequantise warps, one CTA per SM: measured faster at M = 2048 than
   // 128-token tiles with 8 warps and two CTAs per SM (700 vs 595 TFLOP/s).
   a.dw = 16;
-  CUtensorMap wmap, xmap, xmap_lo, omap;
-  memset(&xmap_lo, 0, sizeof(xmap_lo));
-  memset(&omap, 0, sizeof(omap));
-  if (!tensor_map_2d(&wmap, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
-                     (uint64_t)(K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B))
-    return cudaErrorInvalidValue;
   // FP32 activations: split into bf16 hi / lo arrays in stream-ordered scratch.
   void* scratch = nullptr;
   const void* x_hi = x;
@@ -670,28 +749,26 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
     x_lo = static_cast<char*>(scratch) + half_bytes;
   }
   const CUtensorMapDataType xt = x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  bool ok = tensor_map_2d(&xmap, x_hi, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
+  bool ok = tensor_map_2d(&mp.x, x_hi, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
                           CU_TENSOR_MAP_SWIZZLE_128B);
   if (ok && x_lo)
-    ok = tensor_map_2d(&xmap_lo, x_lo, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
+    ok = tensor_map_2d(&mp.x_lo, x_lo, xt, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup, (uint32_t)a.BN,
                        CU_TENSOR_MAP_SWIZZLE_128B);
   cudaError_t e = cudaErrorInvalidValue;
   if (ok) {
-    // Output tile by TMA store when the row pitch allows a tensor map (a
-    // multiple of 16 bytes, 16-byte-aligned base); otherwise direct stores.
-    const int osz = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
-    a.tma_out = a.ksplit == 1 && ((N * osz) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
-                tensor_map_2d(&omap, out,
-                              x_dtype == QI4_DTYPE_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                              : x_dtype == QI4_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                              (uint64_t)N, (uint64_t)M, (uint64_t)N * osz, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
-    e = x_dtype == QI4_DTYPE_F16   ? launch_x<QI4_DTYPE_F16>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
-        : x_dtype == QI4_DTYPE_F32 ? launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, pdl)
-                                   : launch_x<QI4_DTYPE_BF16>(wmap, xmap, xmap_lo, omap, a, stream, pdl);
+    e = x_dtype == QI4_DTYPE_F16   ? launch_x<QI4_DTYPE_F16>(mp, a, stream, pdl)
+        : x_dtype == QI4_DTYPE_F32 ? launch_x<QI4_DTYPE_F32>(mp, a, stream, pdl)
+                                   : launch_x<QI4_DTYPE_BF16>(mp, a, stream, pdl);
   }
   scratch_free(scratch, stream);
   return e;
+}
+
+cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,
+                           const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
+                           int64_t N, cudaStream_t stream, bool pdl, int num_sms) {
+  return launch_gemm_tc_multi(x, x_dtype, M, K, 1, &qweight, &scales, &zeros, &bias, bias_dtype, &out, &N, stream,
+                              pdl, num_sms);
 }
 
 // ---------------------------------------------------------------------------
@@ -747,20 +824,18 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
   void* scratch = nullptr;
   cudaError_t e = static_scratch_address(&scratch);
   if (e != cudaSuccess) return e;
-  Args a;
+  Args a{};
+  Maps mp;
+  memset(&mp, 0, sizeof(mp));
   a.M = (int)M;
-  a.N = N;
   a.K = K;
-  a.scales = reinterpret_cast<const __half*>(scales);
-  a.zeros = zeros;
-  a.bias = bias;
   a.bias_dtype = bias_dtype;
-  a.out = out;
   a.out_dtype = QI4_DTYPE_F32;
+  void* outp = out;
+  if (!set_mats(a, mp, 1, &qweight, &scales, &zeros, &bias, &outp, &N)) return cudaErrorInvalidValue;
   plan_tiles(a, QI4_DTYPE_F32, num_sms);
+  if (a.ksplit > 1) a.tma_out = 0;
   a.dw = 16;
-  CUtensorMap wmap, xmap, xmap_lo, omap;
-  memset(&omap, 0, sizeof(omap));
   // Every element of the hi / lo arrays that the GEMM reads is written by the
   // split pass of the same call, so nothing left from an earlier call is used.
   const int64_t n4 = M * K / 4;
@@ -770,17 +845,12 @@ cudaError_t launch_gemm_tc_f32_static(const float* x, int64_t M, int64_t K, cons
   split_f32_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const float4*>(x), hi, lo, n4);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (!tensor_map_2d(&wmap, qweight, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
-                     (uint64_t)(K / 2), 128, kTileN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !tensor_map_2d(&xmap, hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup,
+  if (!tensor_map_2d(&mp.x, hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kGroup,
                      (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !tensor_map_2d(&xmap_lo, lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
+      !tensor_map_2d(&mp.x_lo, lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2,
                      kGroup, (uint32_t)a.BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  a.tma_out = a.ksplit == 1 && ((N * 4) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
-              tensor_map_2d(&omap, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)N, (uint64_t)M,
-                            (uint64_t)N * 4, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
-  return launch_x<QI4_DTYPE_F32>(wmap, xmap, xmap_lo, omap, a, stream, false);
+  return launch_x<QI4_DTYPE_F32>(mp, a, stream, false);
 }
 
 int read_gemm_tc_error(cudaStream_t stream) {

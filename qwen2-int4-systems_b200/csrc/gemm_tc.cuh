@@ -13,6 +13,14 @@ cudaError_t launch_gemm_tc(const void* x, int x_dtype, int64_t M, int64_t K, con
                            const uint16_t* scales, const uint8_t* zeros, const void* bias, int bias_dtype, void* out,
                            int64_t N, cudaStream_t stream, bool pdl, int num_sms);
 
+// Up to three weight matrices that share the activations (q/k/v, gate/up) in
+// one launch: each CTA takes a 128-row tile of one matrix; every output has
+// the activation dtype.
+cudaError_t launch_gemm_tc_multi(const void* x, int x_dtype, int64_t M, int64_t K, int count,
+                                 const uint8_t* const* qweights, const uint16_t* const* scales,
+                                 const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                 void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl, int num_sms);
+
 // FP32-activation tensor-core linear whose scratch is a fixed static device
 // array (no allocation); x and out are FP32. M * K * 4 bytes must not exceed
 // static_scratch_bytes(). Not reentrant across concurrent streams.

@@ -12,8 +12,10 @@ Each rank computes ``x @ W_r^T`` for its rows with the b200 kernels and the
 shards are joined with one ``all_gather_into_tensor`` over NCCL (NVLink /
 NVSwitch on one node). For the SwiGLU MLP (src/qwen_int4/model.py:125-136)
 gate and up shards line up element-wise, so ``silu(gate) * up`` is formed on
-the shard and gathered once before ``down_proj``, whose output is gathered
-again: two collectives per MLP.
+the shard by the fused gate/up call; ``ColumnParallelMLP`` then either
+gathers it for a column-split ``down_proj`` (two all-gathers per MLP) or
+feeds it to a ``down_proj`` split by input features on the same boundaries
+(one all-reduce of the output, the intermediate never leaves the GPU).
 
 The per-shard compute is pluggable (``linear_fn``) so that the sharding and
 gathering logic can be tested on CPU ranks (gloo) against the oracle; the
@@ -82,6 +84,27 @@ def shard_rows(qweight, scales, zeros, bias, *, in_features: int, start: int, st
                       None if b is None else b.contiguous(), (start, stop), k)
 
 
+def group_bounds(n: int, world: int, rank: int, unit: int = GROUP) -> tuple[int, int]:
+    """Range of ``rank`` with every boundary on a multiple of ``unit`` (whole
+    quantisation groups): ``n`` in ``unit`` blocks split as evenly as possible."""
+    a, b = shard_bounds(-(-n // unit), world, rank)
+    return min(a * unit, n), min(b * unit, n)
+
+
+def shard_cols(qweight, scales, zeros, *, out_features: int, in_features: int, start: int,
+               stop: int) -> W4G64Shard:
+    """Input features [start, stop) of a canonical W4G64 linear (whole groups):
+    the packed bytes, scales and zero points of those groups of every row."""
+    n, k = out_features, in_features
+    if start % GROUP or (stop % GROUP and stop != k) or not 0 <= start <= stop <= k:
+        raise ValueError(f"column shard [{start}, {stop}) must fall on group boundaries of K={k}")
+    g, g0, g1 = k // GROUP, start // GROUP, stop // GROUP
+    q = qweight.reshape(n, k // 2)[:, start // 2: stop // 2]
+    s = scales.reshape(n, g)[:, g0:g1]
+    z = _pack_nibbles(_unpack_nibbles(zeros, n * g).reshape(n, g)[:, g0:g1].reshape(-1)).to(zeros.device)
+    return W4G64Shard(q.contiguous().reshape(-1, 1), s.contiguous(), z.contiguous(), None, (0, n), stop - start)
+
+
 def _default_linear(x, shard: W4G64Shard) -> torch.Tensor:
     from .backends import b200_w4g64_linear
 
@@ -90,19 +113,36 @@ def _default_linear(x, shard: W4G64Shard) -> torch.Tensor:
                              group_size=GROUP, packing="canonical")
 
 
-def gather_columns(local: torch.Tensor, n_total: int, group=None) -> torch.Tensor:
-    """All-gather ``[M, N_r]`` shards (contiguous row ranges) into ``[M, N]``."""
-    world = dist.get_world_size(group)
+def _default_swiglu(x, gate: W4G64Shard, up: W4G64Shard) -> torch.Tensor:
+    from .backends import b200_w4g64_gate_up_silu
+
+    return b200_w4g64_gate_up_silu(x, gate, up)
+
+
+def _world(group) -> tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0  # one process: no collectives
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def gather_columns(local: torch.Tensor, n_total: int, group=None, bounds=None) -> torch.Tensor:
+    """All-gather ``[M, N_r]`` shards (contiguous column ranges, rank order)
+    into ``[M, N]``. ``bounds`` lists every rank's range (default: ``shard_bounds``)."""
+    world, _ = _world(group)
+    if world == 1:
+        return local
     m = local.shape[0]
-    sizes = [shard_bounds(n_total, world, r) for r in range(world)]
+    sizes = bounds or [shard_bounds(n_total, world, r) for r in range(world)]
     width = max(b - a for a, b in sizes)
     if local.shape[1] != width:  # uneven split: pad to a common width
         local = torch.nn.functional.pad(local, (0, width - local.shape[1]))
     buf = torch.empty((world * m, width), dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(buf, local.contiguous(), group=group)  # rank r -> rows [r*M, (r+1)*M)
     buf = buf.view(world, m, width)
-    parts = [buf[r, :, : b - a] for r, (a, b) in enumerate(sizes)]
-    return torch.cat(parts, dim=1)
+    out = torch.empty((m, n_total), dtype=local.dtype, device=local.device)
+    for r, (a, b) in enumerate(sizes):  # one strided copy per rank, no intermediate concatenation
+        out[:, a:b].copy_(buf[r, :, : b - a])
+    return out
 
 
 class ColumnParallelW4G64:
@@ -111,8 +151,7 @@ class ColumnParallelW4G64:
     def __init__(self, qweight, scales, zeros, bias, *, in_features: int, out_features: int,
                  group=None, linear_fn: Callable | None = None):
         self.group = group
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        self.world, self.rank = _world(group)
         self.out_features = out_features
         self.in_features = in_features
         a, b = shard_bounds(out_features, self.world, self.rank)
@@ -133,24 +172,72 @@ class ColumnParallelW4G64:
 
 
 class ColumnParallelMLP:
-    """SwiGLU MLP (src/qwen_int4/model.py:125-136) with gate/up/down column-split.
+    """SwiGLU MLP (src/qwen_int4/model.py:125-136) split over the ranks of ``group``.
 
-    ``silu(gate) * up`` is computed in FP32 on the aligned gate/up shards and
-    gathered once; ``down_proj`` receives the FP32 intermediate, as in the
-    reference, and its output shards are gathered and cast to ``x.dtype``.
+    gate_proj / up_proj are split by output features on whole-group
+    boundaries (64 columns), and each rank forms ``silu(gate) * up`` in FP32
+    on its shard with one fused call (the FP32 tensor the reference passes to
+    ``down_proj``). Then, by ``mode``:
+
+    * ``"column"`` - the intermediate is all-gathered (FP32, M x 8960),
+      ``down_proj`` is split by output features, and its output, cast to
+      ``x.dtype`` first, is all-gathered: two all-gathers per MLP.
+    * ``"column_row"`` - ``down_proj`` is split by input features on the same
+      boundaries, so each rank's intermediate shard is exactly the input its
+      ``down_proj`` shard needs; the FP32 partial outputs are summed with one
+      all-reduce (M x 1536 FP32) and cast. Nothing of the intermediate
+      crosses the link. The sum over ranks changes the FP32 summation order
+      only.
+
+    With one process (no process group) both modes are the unsplit MLP.
     """
 
-    def __init__(self, mlp, group=None, linear_fn=None):
-        self.gate = ColumnParallelW4G64.from_quant_linear(mlp.gate_proj, group, linear_fn)
-        self.up = ColumnParallelW4G64.from_quant_linear(mlp.up_proj, group, linear_fn)
-        self.down = ColumnParallelW4G64.from_quant_linear(mlp.down_proj, group, linear_fn)
-        self.group = group
+    MODES = ("column", "column_row")
+
+    def __init__(self, mlp, group=None, linear_fn=None, mode: str = "column", swiglu_fn=None):
+        if mode not in self.MODES:
+            raise ValueError(f"mode must be one of {self.MODES}, got {mode!r}")
+        self.group, self.mode = group, mode
+        self.world, self.rank = _world(group)
+        gate, up, down = mlp.gate_proj, mlp.up_proj, mlp.down_proj
+        self.hidden, self.inter = gate.in_features, gate.out_features
+        self.bounds = [group_bounds(self.inter, self.world, r) for r in range(self.world)]
+        a, b = self.bounds[self.rank]
+        self.gate = shard_rows(gate.qweight, gate.scales, gate.zeros, None, in_features=self.hidden, start=a, stop=b)
+        self.up = shard_rows(up.qweight, up.scales, up.zeros, None, in_features=self.hidden, start=a, stop=b)
+        if mode == "column":
+            ra, rb = shard_bounds(self.hidden, self.world, self.rank)
+            self.down = shard_rows(down.qweight, down.scales, down.zeros, down.bias, in_features=self.inter,
+                                   start=ra, stop=rb)
+        else:
+            self.down = shard_cols(down.qweight, down.scales, down.zeros, out_features=self.hidden,
+                                   in_features=self.inter, start=a, stop=b)
+            self.down_bias = down.bias
+        self.linear_fn = linear_fn or _default_linear
+        if swiglu_fn is None and linear_fn is not None:
+            swiglu_fn = lambda x, g, u: (torch.nn.functional.silu(self.linear_fn(x, g).float())  # noqa: E731
+                                         * self.linear_fn(x, u).float())
+        self.swiglu_fn = swiglu_fn or _default_swiglu
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
-        g = self.gate.local(x).to(torch.float32)
-        u = self.up.local(x).to(torch.float32)
-        h = torch.nn.functional.silu(g) * u
-        full_h = gather_columns(h, self.gate.out_features, self.group)
-        y = self.down(full_h)
-        return y.reshape(*lead, self.down.out_features).to(x.dtype)
+        x2 = x.reshape(-1, self.hidden)
+        if self.gate.out_features:
+            h = self.swiglu_fn(x2, self.gate, self.up)
+        else:
+            h = torch.zeros((x2.shape[0], 0), dtype=torch.float32, device=x.device)
+        if self.mode == "column":
+            full_h = gather_columns(h, self.inter, self.group, self.bounds)
+            y = self.linear_fn(full_h, self.down).to(x.dtype)
+            y = gather_columns(y, self.hidden, self.group)
+        else:
+            if self.down.in_features:
+                y = self.linear_fn(h, self.down).float()
+            else:
+                y = torch.zeros((x2.shape[0], self.hidden), dtype=torch.float32, device=x.device)
+            if self.world > 1:
+                dist.all_reduce(y, group=self.group)
+            if self.down_bias is not None:
+                y = y + self.down_bias.float()
+            y = y.to(x.dtype)
+        return y.reshape(*lead, self.hidden)

@@ -1,4 +1,8 @@
-"""Column-split W4G64 on 2 GPUs over NCCL (skipped on a single-GPU host)."""
+"""Column-split W4G64 on 2 GPUs over NCCL (skipped on a single-GPU host).
+
+A split linear against the oracle, and the Qwen2 MLP in both split modes
+against the same MLP unsplit on one GPU (the b200 kernels either way).
+"""
 
 import datetime
 import os
@@ -46,6 +50,26 @@ def _worker(rank, world, port, result_path):
             got = lin(x.to(dev)).float().cpu().numpy()
             ref = orc.linear(x.float().numpy(), qw, sc, z, None, out_features=n, in_features=k, accumulate="f64")
             ok = ok and got.shape == ref.shape and bool(np.all(np.abs(got - ref) <= 2e-2 + np.abs(ref) * 2 ** -7))
+        from types import SimpleNamespace
+
+        def qlinear(n, k):
+            qw, sc = orc.quantize_symmetric_rtn(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+            z = np.zeros(((n * (k // 64) + 1) // 2, 1), dtype=np.uint8)
+            return SimpleNamespace(qweight=torch.from_numpy(qw).to(dev), scales=torch.from_numpy(sc).to(dev),
+                                   zeros=torch.from_numpy(z).to(dev), bias=None, in_features=k, out_features=n)
+
+        mlp = SimpleNamespace(gate_proj=qlinear(8960, 1536), up_proj=qlinear(8960, 1536),
+                              down_proj=qlinear(1536, 8960))
+        x = torch.from_numpy(rng.standard_normal((512, 1536), dtype=np.float32)).to(torch.bfloat16).to(dev)
+        b200 = importlib.import_module("qwen2-int4-systems_b200")
+        hm = b200.b200_w4g64_gate_up_silu(x, mlp.gate_proj, mlp.up_proj)
+        d = mlp.down_proj
+        ref = b200.b200_w4g64_linear(hm, d.qweight, d.scales, d.zeros, None, out_features=1536, in_features=8960,
+                                     group_size=64, packing="canonical").to(torch.bfloat16).float()
+        for mode in ("column", "column_row"):
+            got = par.ColumnParallelMLP(mlp, mode=mode)(x).float()
+            cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0)
+            ok = ok and bool((got - ref).abs().max() <= 2e-2 + 2 ** -7 * ref.abs().max()) and float(cos) > 0.99999
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if rank == 0:

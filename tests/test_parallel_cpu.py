@@ -96,7 +96,7 @@ def test_odd_group_count_zero_points_are_repacked():
         np.testing.assert_array_equal(part, full[a:b])
 
 
-def _mlp_worker(rank, world, port, result_path):
+def _mlp_worker(rank, world, port, result_path, mode="column"):
     import importlib
     import sys
     from types import SimpleNamespace
@@ -118,7 +118,7 @@ def _mlp_worker(rank, world, port, result_path):
         mlp = SimpleNamespace(gate_proj=qlinear(inter, hidden), up_proj=qlinear(inter, hidden),
                               down_proj=qlinear(hidden, inter))
         x = torch.from_numpy(rng.standard_normal((4, hidden), dtype=np.float32)).to(torch.bfloat16)
-        got = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear)(x)
+        got = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode=mode)(x)
 
         def full(layer, inp):
             return orc.linear(inp, layer.qweight.numpy(), layer.scales.numpy(), layer.zeros.numpy(), None,
@@ -139,11 +139,61 @@ def _mlp_worker(rank, world, port, result_path):
         dist.destroy_process_group()
 
 
-def test_column_split_swiglu_mlp_matches_unsplit(tmp_path):
+@pytest.mark.parametrize(("mode", "world"), [("column", 2), ("column_row", 2), ("column_row", 3)])
+def test_column_split_swiglu_mlp_matches_unsplit(tmp_path, mode, world):
+    """Both split modes give the unsplit MLP (intermediate 320 = 5 groups, so
+    3 ranks get uneven group-aligned shards)."""
     result = tmp_path / "ok"
-    mp.start_processes(_mlp_worker, args=(2, _free_port(), str(result)), nprocs=2, join=True,
+    mp.start_processes(_mlp_worker, args=(world, _free_port(), str(result), mode), nprocs=world, join=True,
                        start_method="spawn")
     assert result.read_text() == "1"
+
+
+def test_single_process_mlp_is_the_unsplit_mlp():
+    """Without a process group both modes run the whole MLP on one rank."""
+    import importlib
+    from types import SimpleNamespace
+
+    par = importlib.import_module("qwen2-int4-systems_b200.parallel")
+    rng = np.random.default_rng(3)
+
+    def qlinear(n, k):
+        qw, sc, z = orc.quantize_asymmetric_rtn(rng.standard_normal((n, k), dtype=np.float32) * 0.05)
+        return SimpleNamespace(qweight=torch.from_numpy(qw), scales=torch.from_numpy(sc),
+                               zeros=torch.from_numpy(z), bias=None, in_features=k, out_features=n)
+
+    mlp = SimpleNamespace(gate_proj=qlinear(192, 64), up_proj=qlinear(192, 64), down_proj=qlinear(64, 192))
+    x = torch.from_numpy(rng.standard_normal((2, 64), dtype=np.float32)).to(torch.bfloat16)
+    a = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode="column")(x)
+    b = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode="column_row")(x)
+    assert torch.equal(a, b)
+
+
+def test_group_bounds_and_column_shards():
+    """Group-aligned ranges cover the features exactly, and a column shard
+    dequantises to the matching columns of the full weight (odd G: zero
+    points repacked)."""
+    import importlib
+
+    par = importlib.import_module("qwen2-int4-systems_b200.parallel")
+    for n, world in ((8960, 8), (8960, 3), (320, 3), (64, 2), (1536, 8)):
+        spans = [par.group_bounds(n, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert all(a % 64 == 0 for a, _ in spans)
+    rng = np.random.default_rng(4)
+    n, k = 5, 320  # G = 5
+    qw, sc, z = orc.quantize_asymmetric_rtn(rng.standard_normal((n, k), dtype=np.float32))
+    full = orc.dequantize_groupwise(qw, sc, out_features=n, in_features=k, zeros=z)
+    for a, b in ((0, 128), (128, 320), (64, 192)):
+        sh = par.shard_cols(torch.from_numpy(qw), torch.from_numpy(sc), torch.from_numpy(z),
+                            out_features=n, in_features=k, start=a, stop=b)
+        part = orc.dequantize_groupwise(sh.qweight.numpy(), sh.scales.numpy(), out_features=n,
+                                        in_features=b - a, zeros=sh.zeros.numpy())
+        np.testing.assert_array_equal(part, full[:, a:b])
+    with pytest.raises(ValueError):
+        par.shard_cols(torch.from_numpy(qw), torch.from_numpy(sc), torch.from_numpy(z),
+                       out_features=n, in_features=k, start=32, stop=128)
 
 
 def _dead_peer_worker(rank, world, port, result_path):
