@@ -677,10 +677,31 @@ def reference_harness_decode(device, prompt_len: int = 512, new_tokens: int = 12
             lb = model(prompt).float()
             model.set_backend("torch")
             lt = model(prompt).float()
-        cos_last = torch.nn.functional.cosine_similarity(lb[0, -1], lt[0, -1], dim=0)
-        cos_all = torch.nn.functional.cosine_similarity(lb.flatten(), lt.flatten(), dim=0)
-        result["final_logits_cosine_vs_torch_backend"] = {"last_position": float(cos_last),
-                                                          "all_positions": float(cos_all)}
+            # The reference's own spread: its torch path with the matmul in
+            # float64 instead of float32, against itself.
+            import qwen_int4.linear as ref_linear
+            from qwen_int4.quantization import dequantize_groupwise
+
+            def forward_f64(self, x):
+                w = dequantize_groupwise(self.qweight, self.scales, zeros=self.zeros, out_features=self.out_features,
+                                         in_features=self.in_features, group_size=self.group_size,
+                                         packing=self.packing)
+                out = (x.reshape(-1, self.in_features).double() @ w.double().t()).float()
+                if self.bias is not None:
+                    out = out + self.bias.float()
+                return out.reshape(*x.shape[:-1], self.out_features).to(x.dtype)
+
+            saved = ref_linear.QuantLinear.forward
+            ref_linear.QuantLinear.forward = forward_f64
+            try:
+                l64 = model(prompt).float()
+            finally:
+                ref_linear.QuantLinear.forward = saved
+        cos = lambda a, b: float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0))  # noqa: E731
+        result["final_logits_cosine_vs_torch_backend"] = {
+            "last_position": cos(lb[0, -1], lt[0, -1]), "all_positions": cos(lb, lt),
+            "reference_f64_vs_f32_last_position": cos(l64[0, -1], lt[0, -1]),
+            "reference_f64_vs_f32_all_positions": cos(l64, lt), "north_star": 0.9999}
     finally:
         q2.register_with_reference(ref.__name__, fast_attention=False)
         torch.backends.cuda.enable_cudnn_sdp(cudnn_sdp)
