@@ -242,6 +242,43 @@ QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const voi
                                      void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
                                      void* stream);
 
+/* Residual add + RMSNorm at a decoder block boundary (the reference's
+ * DecoderLayer / RMSNorm, src/qwen_int4/model.py:31-42,151-159), in place on
+ * the bf16 residual stream h [B, D]:
+ *   h   = bf16(h + bf16(delta))   (delta [B, D] of BF16 or F32; NULL: none)
+ *   out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * weight)   (FP32 statistics)
+ * D <= 4096. No reference counterpart as a single call. */
+QI4_API int qi4_add_rmsnorm(void* h, const void* delta, int delta_dtype, const void* weight, void* out, int64_t B,
+                            int64_t D, float eps, void* stream);
+
+/* The same block boundary folded into the next linear's activation staging
+ * (decode sizes, bf16): the launch forms x = bf16(bf16(hn * rsqrt(mean(hn^2)
+ * + eps)) * weight) from hn = bf16(h_in + bf16(delta)) itself, one launch
+ * fewer per boundary, and writes hn to h_out. h_out must not overlap h_in
+ * (callers alternate two residual buffers). */
+typedef struct qi4_rmsnorm_prologue {
+  const void* h_in;     /* bf16 [M, K] residual stream in */
+  const void* delta;    /* BF16 or F32 [M, K] block output added to it, or NULL */
+  int32_t delta_dtype;  /* QI4_DTYPE_BF16 or QI4_DTYPE_F32 */
+  float eps;
+  const void* weight;   /* bf16 [K] RMSNorm weight */
+  void* h_out;          /* bf16 [M, K] residual stream out */
+} qi4_rmsnorm_prologue;
+
+/* qi4_w4g64_linear_multi with x formed by `norm` (bf16; 1 <= M <= 16; all
+ * pointers of `norm` 16-byte aligned). */
+QI4_API int qi4_w4g64_linear_multi_norm(const qi4_rmsnorm_prologue* norm, int64_t M, int64_t K, int count,
+                                        const uint8_t* const* qweights, const uint16_t* const* scales_f16,
+                                        const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                        void* const* outs, const int64_t* Ns, void* stream);
+
+/* qi4_w4g64_gate_up_silu with x formed by `norm` (same conditions). */
+QI4_API int qi4_w4g64_gate_up_silu_norm(const qi4_rmsnorm_prologue* norm, int64_t M, int64_t K,
+                                        const uint8_t* qweight_gate, const uint16_t* scales_gate_f16,
+                                        const uint8_t* zeros_gate, const uint8_t* qweight_up,
+                                        const uint16_t* scales_up_f16, const uint8_t* zeros_up, float* out,
+                                        int64_t N, void* stream);
+
 /*
  * Tied bf16 lm_head for decode sizes: logits[M, N] = x[M, K] @ W[N, K]^T
  * (bf16 in, FP32 sums, bf16 out - the reference's nn.Linear lm_head over the
@@ -252,15 +289,6 @@ QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const voi
  * token skips writing the logits. 1 <= M <= 8, K a multiple of 8 (<= 16384),
  * weight and x 16-byte aligned. No reference counterpart as a single call.
  */
-/* Residual add + RMSNorm at a decoder block boundary (the reference's
- * DecoderLayer / RMSNorm, src/qwen_int4/model.py:31-42,151-159), in place on
- * the bf16 residual stream h [B, D]:
- *   h   = bf16(h + bf16(delta))   (delta [B, D] of BF16 or F32; NULL: none)
- *   out = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * weight)   (FP32 statistics)
- * D <= 4096. No reference counterpart as a single call. */
-QI4_API int qi4_add_rmsnorm(void* h, const void* delta, int delta_dtype, const void* weight, void* out, int64_t B,
-                            int64_t D, float eps, void* stream);
-
 QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
                                  int64_t* argmax, void* stream);
 

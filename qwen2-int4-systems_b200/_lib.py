@@ -42,11 +42,22 @@ SIGNATURES = {
                                  _i64, _i64, ctypes.c_float, _p],
     "qi4_bf16_gemv_argmax": [_p, _p, _i64, _i64, _i64, _p, _p, _p],
     "qi4_add_rmsnorm": [_p, _p, _i, _p, _p, _i64, _i64, ctypes.c_float, _p],
+    "qi4_w4g64_linear_multi_norm": [_p, _i64, _i64, _i, _p, _p, _p, _p, _i, _p, _p, _p],
+    "qi4_w4g64_gate_up_silu_norm": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
     "qi4_last_error": [ctypes.c_char_p, _sz],
     "qi4_version": [],
 }
 
 CHAIN_SWIGLU = 1
+
+
+class RmsNormPrologue(ctypes.Structure):
+    """``qi4_rmsnorm_prologue`` of include/qi4_b200.h."""
+
+    _fields_ = [
+        ("h_in", ctypes.c_void_p), ("delta", ctypes.c_void_p), ("delta_dtype", ctypes.c_int32),
+        ("eps", ctypes.c_float), ("weight", ctypes.c_void_p), ("h_out", ctypes.c_void_p),
+    ]
 
 
 class ChainStage(ctypes.Structure):

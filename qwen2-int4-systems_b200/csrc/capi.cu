@@ -244,11 +244,52 @@ static int linear_impl(const void* x, int x_dtype, int64_t M, int64_t K, const u
   return QI4_OK;
 }
 
+// Checks a fused norm prologue and converts it; x of the launch is then h_in.
+static int validate_norm(const qi4_rmsnorm_prologue* n, int64_t M, int64_t K, NormPrologue* out) {
+  if (!n || !n->h_in || !n->weight || !n->h_out) {
+    set_error("the norm prologue and its h_in, weight and h_out must be non-null");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (M < 1 || M > kGemvMaxM) {
+    set_error("the fused norm prologue covers 1..%d tokens (got M=%lld)", kGemvMaxM, (long long)M);
+    return QI4_ERR_SHAPE;
+  }
+  if (n->delta && n->delta_dtype != QI4_DTYPE_BF16 && n->delta_dtype != QI4_DTYPE_F32) {
+    set_error("norm delta dtype %d is not BF16 or F32", n->delta_dtype);
+    return QI4_ERR_DTYPE;
+  }
+  if (!aligned(n->h_in, 16) || !aligned(n->h_out, 16) || !aligned(n->weight, 16) ||
+      (n->delta && !aligned(n->delta, 16))) {
+    set_error("norm h_in, delta, weight and h_out must be 16-byte aligned");
+    return QI4_ERR_ALIGNMENT;
+  }
+  const uintptr_t a = reinterpret_cast<uintptr_t>(n->h_in), b = reinterpret_cast<uintptr_t>(n->h_out);
+  const uintptr_t bytes = (uintptr_t)(M * K * 2);
+  if (a < b + bytes && b < a + bytes) {
+    set_error("norm h_out must not overlap h_in (alternate two residual buffers)");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (!(n->eps >= 0.f) || n->eps > 1.f) {
+    set_error("norm eps must be in [0, 1]");
+    return QI4_ERR_ARGUMENT;
+  }
+  *out = NormPrologue{n->h_in, n->delta, n->delta_dtype, n->eps, n->weight, n->h_out};
+  return QI4_OK;
+}
+
 static int linear_multi_impl(const void* x, int x_dtype, int64_t M, int64_t K, int count,
                              const uint8_t* const* qweights, const uint16_t* const* scales,
                              const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
-                             void* const* outs, const int64_t* Ns, void* stream_ptr) {
+                             void* const* outs, const int64_t* Ns, void* stream_ptr,
+                             const qi4_rmsnorm_prologue* norm = nullptr) {
   clear_error();
+  NormPrologue np{};
+  if (norm) {
+    const int rc = validate_norm(norm, M, K, &np);
+    if (rc) return rc;
+    x = norm->h_in;
+    x_dtype = QI4_DTYPE_BF16;
+  }
   if (count < 1 || count > 3 || !qweights || !scales || !outs || !Ns) {
     set_error("count must be 1..3 and qweights, scales, outs, Ns non-null host arrays");
     return QI4_ERR_ARGUMENT;
@@ -284,14 +325,22 @@ static int linear_multi_impl(const void* x, int x_dtype, int64_t M, int64_t K, i
     return QI4_ERR_SHAPE;
   }
   return check_launch(launch_gemv_mma_multi(x, x_dtype, M, K, count, qweights, scales, zs, bs, bias_dtype, outs, Ns,
-                                            static_cast<cudaStream_t>(stream_ptr), true, plan),
+                                            static_cast<cudaStream_t>(stream_ptr), true, plan, norm ? &np : nullptr),
                       "w4g64 grouped GEMV");
 }
 
 static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qw_gate,
                              const uint16_t* sc_gate, const uint8_t* z_gate, const uint8_t* qw_up,
-                             const uint16_t* sc_up, const uint8_t* z_up, float* out, int64_t N, void* stream_ptr) {
+                             const uint16_t* sc_up, const uint8_t* z_up, float* out, int64_t N, void* stream_ptr,
+                             const qi4_rmsnorm_prologue* norm = nullptr) {
   clear_error();
+  NormPrologue np{};
+  if (norm) {
+    const int rc = validate_norm(norm, M, K, &np);
+    if (rc) return rc;
+    x = norm->h_in;
+    x_dtype = QI4_DTYPE_BF16;
+  }
   int rc = validate_linear(x, x_dtype, M, K, qw_gate, sc_gate, nullptr, QI4_DTYPE_NONE, out, N);
   if (!rc) rc = validate_linear(x, x_dtype, M, K, qw_up, sc_up, nullptr, QI4_DTYPE_NONE, out, N);
   if (rc) return rc;
@@ -312,7 +361,8 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
       set_error("no fused gate/up launch shape fits K=%lld", (long long)K);
       return QI4_ERR_SHAPE;
     }
-    return check_launch(launch_gemv_swiglu(x, x_dtype, M, K, qws, scs, zs, out, N, stream, true, plan),
+    return check_launch(launch_gemv_swiglu(x, x_dtype, M, K, qws, scs, zs, out, N, stream, true, plan,
+                                           norm ? &np : nullptr),
                         "w4g64 fused gate/up SwiGLU GEMV");
   }
   // Prefill sizes: both projections in one tensor-core launch into scratch
@@ -358,6 +408,33 @@ int qi4_w4g64_linear_multi(const void* x, int x_dtype, int64_t M, int64_t K, int
                            void* const* outs, const int64_t* Ns, void* stream) {
   return linear_multi_impl(x, x_dtype, M, K, count, qweights, scales_f16, zeros, biases, bias_dtype, outs, Ns,
                            stream);
+}
+
+int qi4_w4g64_linear_multi_norm(const qi4_rmsnorm_prologue* norm, int64_t M, int64_t K, int count,
+                                const uint8_t* const* qweights, const uint16_t* const* scales_f16,
+                                const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
+                                void* const* outs, const int64_t* Ns, void* stream) {
+  if (!norm) {
+    clear_error();
+    set_error("the norm prologue must be non-null");
+    return QI4_ERR_ARGUMENT;
+  }
+  return linear_multi_impl(norm->h_in, QI4_DTYPE_BF16, M, K, count, qweights, scales_f16, zeros, biases, bias_dtype,
+                           outs, Ns, stream, norm);
+}
+
+int qi4_w4g64_gate_up_silu_norm(const qi4_rmsnorm_prologue* norm, int64_t M, int64_t K,
+                                const uint8_t* qweight_gate, const uint16_t* scales_gate_f16,
+                                const uint8_t* zeros_gate, const uint8_t* qweight_up,
+                                const uint16_t* scales_up_f16, const uint8_t* zeros_up, float* out, int64_t N,
+                                void* stream) {
+  if (!norm) {
+    clear_error();
+    set_error("the norm prologue must be non-null");
+    return QI4_ERR_ARGUMENT;
+  }
+  return gate_up_silu_impl(norm->h_in, QI4_DTYPE_BF16, M, K, qweight_gate, scales_gate_f16, zeros_gate, qweight_up,
+                           scales_up_f16, zeros_up, out, N, stream, norm);
 }
 
 int qi4_w4g64_linear(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight,

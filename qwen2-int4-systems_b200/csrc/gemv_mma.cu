@@ -75,6 +75,8 @@ struct Args {
   int copy_log2;        // log2 of the 128-byte boxes fetched per TMA copy
   int three_d;          // 1: 3-D box-major copies (rows of K/2 bytes a multiple of 128); 0: 2-D, one box each
   int G;                // groups per row (K / 64)
+  int has_norm;         // 1: x is formed from `norm` while staging (bf16 activations)
+  NormPrologue norm;
 };
 
 struct TableEntry {
@@ -268,6 +270,89 @@ __device__ __forceinline__ void stage_x(const Args& a, uint8_t* xs, int xstride,
   }
 }
 
+// The decoder-block boundary folded into the staging (bf16 activations):
+// hn = bf16(h_in + bf16(delta)) (delta absent: hn = h_in), then
+// x = bf16(bf16(hn * rsqrt(mean(hn^2) + eps)) * w), the reference's residual
+// add and RMSNorm (src/qwen_int4/model.py:31-42,151-159) with FP32
+// statistics. Every CTA sums its tokens' whole rows (from L2), then forms
+// and stages its own K slice; the CTAs of the first row tile (blockIdx.x ==
+// 0: one per K slice) also write hn to h_out, which must not alias h_in
+// (other CTAs still read h_in).
+__device__ __forceinline__ void residual8(const NormPrologue& nm, int64_t e, float (&v)[8]) {
+  const uint4 hw = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(nm.h_in) + e));
+  const uint32_t hs[4] = {hw.x, hw.y, hw.z, hw.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    v[2 * q] = __uint_as_float(hs[q] << 16);
+    v[2 * q + 1] = __uint_as_float(hs[q] & 0xFFFF0000u);
+  }
+  if (nm.delta == nullptr) return;
+  float d[8];
+  if (nm.delta_dtype == QI4_DTYPE_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(nm.delta) + e));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(nm.delta) + e) + 1);
+    const float t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = __bfloat162float(__float2bfloat16_rn(t[j]));
+  } else {
+    const uint4 dw = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(nm.delta) + e));
+    const uint32_t ds[4] = {dw.x, dw.y, dw.z, dw.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      d[2 * q] = __uint_as_float(ds[q] << 16);
+      d[2 * q + 1] = __uint_as_float(ds[q] & 0xFFFF0000u);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j] + d[j]));
+}
+
+__device__ __forceinline__ void stage_x_norm(const Args& a, uint8_t* xs, int xstride, int g0, int gs, int tid,
+                                             int nthreads, float* rs) {
+  const NormPrologue& nm = a.norm;
+  const int K = (int)a.K, chunks = K / 8;
+  const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+  for (int tok = warp; tok < a.M; tok += nw) {
+    float ss = 0.f;
+    for (int c = lane; c < chunks; c += 32) {
+      float v[8];
+      residual8(nm, (int64_t)tok * K + c * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) rs[tok] = rsqrtf(ss / (float)K + nm.eps);
+  }
+  __syncthreads();
+  const int per_tok = gs * 8;  // 8-element chunks of the slice per token
+  const uint32_t base = smem_addr(xs);
+  const bool write_h = blockIdx.x == 0;
+  const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(nm.weight);
+  for (int i = tid; i < a.M * per_tok; i += nthreads) {
+    const int tok = i / per_tok, c = i - tok * per_tok;
+    const int64_t k0 = (int64_t)g0 * kGroup + c * 8;
+    float v[8];
+    residual8(nm, (int64_t)tok * K + k0, v);
+    const uint4 ww = __ldg(reinterpret_cast<const uint4*>(w + k0));
+    const uint32_t wv[4] = {ww.x, ww.y, ww.z, ww.w};
+    const float r = rs[tok];
+    uint32_t xo[4], ho[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float n0 = __bfloat162float(__float2bfloat16_rn(v[2 * q] * r));
+      const float n1 = __bfloat162float(__float2bfloat16_rn(v[2 * q + 1] * r));
+      xo[q] = pack_bf16x2(n0 * __uint_as_float(wv[q] << 16), n1 * __uint_as_float(wv[q] & 0xFFFF0000u));
+      ho[q] = pack_bf16x2(v[2 * q], v[2 * q + 1]);  // exact: v holds bf16 values
+    }
+    if (write_h)
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(nm.h_out) + (int64_t)tok * K + k0) =
+          make_uint4(ho[0], ho[1], ho[2], ho[3]);
+    sts128(base + tok * xstride + c * 16, make_uint4(prmt_lo(xo[0], xo[2]), prmt_hi(xo[0], xo[2]),
+                                                     prmt_lo(xo[1], xo[3]), prmt_hi(xo[1], xo[3])));
+  }
+}
+
 __host__ __device__ constexpr int alloc_boxes(int bps, int copy_log2) {
   return ((bps + (1 << copy_log2) - 1) >> copy_log2) << copy_log2;
 }
@@ -416,6 +501,7 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
   // Offset from the shared array itself (not an integer round trip), so that
   // every pointer derived from it stays in the shared address space.
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  __shared__ float norm_rs[16];  // per-token RMSNorm factors of a fused norm prologue (M <= 16)
   constexpr int kWarpsLog2 = WARPS == 32 ? 5 : WARPS == 16 ? 4 : WARPS == 8 ? 3 : WARPS == 4 ? 2 : WARPS == 2 ? 1 : 0;
   static_assert((1 << kWarpsLog2) == WARPS, "warps per CTA must be a power of two");
   const int R = a.rows;
@@ -525,14 +611,20 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
       }
     }
     wait_prerequisites(tid);  // activations come from the previous kernel
-    stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
+    if (XT == QI4_DTYPE_BF16 && a.has_norm)
+      stage_x_norm(a, xs, xstride, g0, gs, tid, kThr, norm_rs);
+    else
+      stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < PRE; ++j)
       if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, x_row, gs);
   } else {
     wait_prerequisites(tid);  // activations come from the previous kernel
-    stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
+    if (XT == QI4_DTYPE_BF16 && a.has_norm)
+      stage_x_norm(a, xs, xstride, g0, gs, tid, kThr, norm_rs);
+    else
+      stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
     __syncthreads();
 
     if (KP % 4 == 0 && gs <= 4 * KP) {
@@ -805,8 +897,9 @@ cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t
                                   const uint8_t* const* qweights, const uint16_t* const* scales,
                                   const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
                                   void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl,
-                                  const MmaGemvPlan& p) {
+                                  const MmaGemvPlan& p, const NormPrologue* norm) {
   if (count < 1 || count > kMaxMats) return cudaErrorInvalidValue;
+  if (norm && (x_dtype != QI4_DTYPE_BF16 || M > 16)) return cudaErrorInvalidValue;
   CUtensorMap maps[kMaxMats];
   Args a{};
   a.x = x;
@@ -820,6 +913,8 @@ cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t
   a.copy_log2 = p.copy_log2;
   a.three_d = p.three_d;
   a.G = (int)(K / kGroup);
+  a.has_norm = norm != nullptr;
+  if (norm) a.norm = *norm;
   int64_t tiles = 0;
   for (int i = 0; i < kMaxMats; ++i) {
     const int j = i < count ? i : count - 1;  // unused slots repeat the last matrix
@@ -894,7 +989,8 @@ MmaGemvPlan plan_gemv_swiglu(int64_t M, int64_t K, int x_dtype) {
 
 cudaError_t launch_gemv_swiglu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* const* qweights,
                                const uint16_t* const* scales, const uint8_t* const* zeros, float* out, int64_t N,
-                               cudaStream_t stream, bool pdl, const MmaGemvPlan& p) {
+                               cudaStream_t stream, bool pdl, const MmaGemvPlan& p, const NormPrologue* norm) {
+  if (norm && (x_dtype != QI4_DTYPE_BF16 || M > 16)) return cudaErrorInvalidValue;
   CUtensorMap maps[kMaxMats];
   for (int i = 0; i < 2; ++i)
     if (!tensor_map_2d(&maps[i], qweights[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2), (uint64_t)N,
@@ -913,6 +1009,8 @@ cudaError_t launch_gemv_swiglu(const void* x, int x_dtype, int64_t M, int64_t K,
   a.copy_log2 = 0;
   a.three_d = 0;
   a.G = (int)(K / kGroup);
+  a.has_norm = norm != nullptr;
+  if (norm) a.norm = *norm;
   const int tiles = (int)((N + 15) / 16);
   for (int i = 0; i < kMaxMats; ++i) {
     const int j = i < 2 ? i : 1;

@@ -7,6 +7,18 @@
 
 namespace qi4 {
 
+// Residual add + RMSNorm formed while a launch stages its activations (bf16
+// only): hn = bf16(h_in + bf16(delta)), x = bf16(bf16(hn * rsqrt(mean(hn^2) +
+// eps)) * weight); hn is written to h_out (which must not alias h_in).
+struct NormPrologue {
+  const void* h_in;    // bf16 [M, K]
+  const void* delta;   // bf16 or FP32 [M, K]; null: hn = h_in
+  int delta_dtype;
+  float eps;
+  const void* weight;  // bf16 [K]
+  void* h_out;         // bf16 [M, K]
+};
+
 struct MmaGemvPlan {
   int rows;             // output rows per CTA: 16, 32, 64 or 128
   int ksplit;           // CTAs per cluster along K (1..8)
@@ -32,14 +44,15 @@ cudaError_t launch_gemv_mma_multi(const void* x, int x_dtype, int64_t M, int64_t
                                   const uint8_t* const* qweights, const uint16_t* const* scales,
                                   const uint8_t* const* zeros, const void* const* biases, int bias_dtype,
                                   void* const* outs, const int64_t* Ns, cudaStream_t stream, bool pdl,
-                                  const MmaGemvPlan& plan);
+                                  const MmaGemvPlan& plan, const NormPrologue* norm = nullptr);
 // Fused gate/up + SwiGLU for M <= 16: out[M, N] (FP32) = silu(g) * u with g, u
 // the two projections of x rounded to the activation dtype (the reference
 // MLP's composition). qweights/scales/zeros hold {gate, up}.
 MmaGemvPlan plan_gemv_swiglu(int64_t M, int64_t K, int x_dtype);
 cudaError_t launch_gemv_swiglu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* const* qweights,
                                const uint16_t* const* scales, const uint8_t* const* zeros, float* out, int64_t N,
-                               cudaStream_t stream, bool pdl, const MmaGemvPlan& plan);
+                               cudaStream_t stream, bool pdl, const MmaGemvPlan& plan,
+                               const NormPrologue* norm = nullptr);
 // out[i] = silu(g[i]) * u[i] in FP32 from two activation-dtype arrays.
 cudaError_t launch_swiglu_elementwise(const void* g, const void* u, int dtype, float* out, int64_t n,
                                       cudaStream_t stream, int num_sms);

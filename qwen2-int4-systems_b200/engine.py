@@ -8,11 +8,14 @@ same model (its QuantLinear buffers, norms, rotary table and tied embedding,
 read as they are) and runs each decode step as one CUDA graph of this
 library's kernels, on static buffers:
 
-  embed -> per layer: residual add + RMSNorm (qi4_add_rmsnorm),
-           q/k/v (qi4_w4g64_linear_multi), RoPE + KV append + GQA attention
-           (qi4_gqa_decode_attention), o_proj (qi4_w4g64_linear),
-           residual add + RMSNorm, gate/up + SwiGLU (qi4_w4g64_gate_up_silu,
-           FP32 out), down_proj (qi4_w4g64_linear on FP32 input)
+  embed -> per layer: residual add + RMSNorm and q/k/v in one launch
+           (qi4_w4g64_linear_multi_norm: the GEMV forms its activations from
+           the residual stream while staging them; up to 16 sequences, else
+           qi4_add_rmsnorm + qi4_w4g64_linear_multi), RoPE + KV append + GQA
+           attention (qi4_gqa_decode_attention), o_proj (qi4_w4g64_linear),
+           residual add + RMSNorm and gate/up + SwiGLU in one launch
+           (qi4_w4g64_gate_up_silu_norm, FP32 out), down_proj
+           (qi4_w4g64_linear on FP32 input)
         -> final residual add + RMSNorm -> tied lm_head + greedy argmax
            (qi4_bf16_gemv_argmax for up to 8 sequences; a bf16 matmul and
            argmax beyond) -> next tokens, lengths and positions advanced on
@@ -83,7 +86,11 @@ class DecodeEngine:
         B = self.B
         # Static buffers of a step.
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.h = torch.empty(B, self.D, **bf)
+        # The bf16 residual stream: with the norm folded into the next launch
+        # (up to 16 sequences) each boundary reads one buffer and writes the
+        # other; otherwise the norm kernel updates hbuf[0] in place.
+        self.hbuf = [torch.empty(B, self.D, **bf), torch.empty(B, self.D, **bf)]
+        self.fuse_norm = B <= 16
         self.x = torch.empty(B, self.D, **bf)
         self.q = torch.empty(B, self.Hq * self.hd, **bf)
         self.k = torch.empty(B, self.Hkv * self.hd, **bf)
@@ -114,27 +121,38 @@ class DecodeEngine:
                                        BF16 if lin.bias is not None else NONE, out.data_ptr(), lin.n, self._s)
         _lib.check(rc, "qi4_w4g64_linear")
 
-    def _norm(self, delta, delta_dtype, w):
-        rc = self.lib.qi4_add_rmsnorm(self.h.data_ptr(), _ptr(delta), delta_dtype, w.data_ptr(), self.x.data_ptr(),
+    def _norm(self, h, delta, delta_dtype, w):
+        rc = self.lib.qi4_add_rmsnorm(h.data_ptr(), _ptr(delta), delta_dtype, w.data_ptr(), self.x.data_ptr(),
                                       self.B, self.D, self.eps, self._s)
         _lib.check(rc, "qi4_add_rmsnorm")
+
+    def _prologue(self, delta, delta_dtype, w):
+        """The boundary folded into the next launch: hbuf[cur] + delta -> hbuf[cur ^ 1]."""
+        src, dst = self.hbuf[self._cur], self.hbuf[self._cur ^ 1]
+        self._cur ^= 1
+        return _lib.RmsNormPrologue(src.data_ptr(), _ptr(delta), delta_dtype, self.eps, w.data_ptr(), dst.data_ptr())
 
     def _step(self):
         B, L = self.B, self.lib
         self._s = torch.cuda.current_stream().cuda_stream
         # The new token is a valid key at position lengths[b].
         self.key_mask.scatter_(1, self.lengths.view(B, 1).long(), 1)
-        torch.index_select(self.embed, 0, self.tokens, out=self.h)
+        self._cur = 0
+        torch.index_select(self.embed, 0, self.tokens, out=self.hbuf[0])
         delta, ddt = None, NONE
         for li, lay in enumerate(self.layers):
-            self._norm(delta, ddt, lay["w_in"])
             qkv = lay["qkv"]
             arr = lambda vals: (ctypes.c_void_p * 3)(*vals)  # noqa: E731
-            rc = L.qi4_w4g64_linear_multi(
-                self.x.data_ptr(), BF16, B, self.D, 3, arr([m.qweight.data_ptr() for m in qkv]),
-                arr([m.scales.data_ptr() for m in qkv]), arr([_ptr(m.zeros) for m in qkv]),
-                arr([_ptr(m.bias) for m in qkv]), BF16, arr([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()]),
-                (ctypes.c_int64 * 3)(*[m.n for m in qkv]), self._s)
+            mats = (3, arr([m.qweight.data_ptr() for m in qkv]), arr([m.scales.data_ptr() for m in qkv]),
+                    arr([_ptr(m.zeros) for m in qkv]), arr([_ptr(m.bias) for m in qkv]), BF16,
+                    arr([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()]),
+                    (ctypes.c_int64 * 3)(*[m.n for m in qkv]), self._s)
+            if self.fuse_norm:
+                pro = self._prologue(delta, ddt, lay["w_in"])
+                rc = L.qi4_w4g64_linear_multi_norm(ctypes.byref(pro), B, self.D, *mats)
+            else:
+                self._norm(self.hbuf[0], delta, ddt, lay["w_in"])
+                rc = L.qi4_w4g64_linear_multi(self.x.data_ptr(), BF16, B, self.D, *mats)
             _lib.check(rc, "qi4_w4g64_linear_multi")
             kc, vc = self.kcache[li], self.vcache[li]
             rc = L.qi4_gqa_decode_attention(
@@ -144,15 +162,19 @@ class DecodeEngine:
                 self.Hq, self.Hkv, self.hd, float(self.hd ** -0.5), self._s)
             _lib.check(rc, "qi4_gqa_decode_attention")
             self._linear(lay["o"], self.attn, BF16, self.o)
-            self._norm(self.o, BF16, lay["w_post"])
             g, u = lay["gate"], lay["up"]
-            rc = L.qi4_w4g64_gate_up_silu(self.x.data_ptr(), BF16, B, self.D, g.qweight.data_ptr(),
-                                          g.scales.data_ptr(), _ptr(g.zeros), u.qweight.data_ptr(),
-                                          u.scales.data_ptr(), _ptr(u.zeros), self.hm.data_ptr(), g.n, self._s)
+            mats = (g.qweight.data_ptr(), g.scales.data_ptr(), _ptr(g.zeros), u.qweight.data_ptr(),
+                    u.scales.data_ptr(), _ptr(u.zeros), self.hm.data_ptr(), g.n, self._s)
+            if self.fuse_norm:
+                pro = self._prologue(self.o, BF16, lay["w_post"])
+                rc = L.qi4_w4g64_gate_up_silu_norm(ctypes.byref(pro), B, self.D, *mats)
+            else:
+                self._norm(self.hbuf[0], self.o, BF16, lay["w_post"])
+                rc = L.qi4_w4g64_gate_up_silu(self.x.data_ptr(), BF16, B, self.D, *mats)
             _lib.check(rc, "qi4_w4g64_gate_up_silu")
             self._linear(lay["down"], self.hm, F32, self.y)
             delta, ddt = self.y, F32
-        self._norm(delta, ddt, self.w_final)
+        self._norm(self.hbuf[self._cur], delta, ddt, self.w_final)
         if B <= 8:
             rc = L.qi4_bf16_gemv_argmax(self.lm_weight.data_ptr(), self.x.data_ptr(), B, self.D,
                                         self.lm_weight.shape[0], None, self.next.data_ptr(), self._s)

@@ -133,3 +133,22 @@ def test_bounded_wait_selftest_validates_its_limit_without_a_gpu(b200):
     _, lib = _lib(b200)
     for bad in (0, 999, 1_000_000_001, 2**63):
         assert lib.qi4_selftest_bounded_wait(bad, None) == -1
+
+
+def test_fused_norm_entry_points_validate_before_any_launch(b200):
+    """The norm-prologue calls reject bad descriptors on the host (no GPU needed)."""
+    mod, lib = _lib(b200)
+    lm = __import__("importlib").import_module(b200.__name__ + "._lib")
+    one = (ctypes.c_void_p * 1)(16)
+    ns = (ctypes.c_int64 * 1)(64)
+    assert lib.qi4_w4g64_linear_multi_norm(None, 1, 64, 1, one, one, one, one, -1, one, ns, None) == -1
+    base = 1 << 20
+    overlap = lm.RmsNormPrologue(base, None, -1, 1e-6, base + 4096, base + 64)  # h_out inside h_in
+    assert lib.qi4_w4g64_linear_multi_norm(ctypes.byref(overlap), 1, 64, 1, one, one, one, one, -1, one, ns, None) == -1
+    big = lm.RmsNormPrologue(base, None, -1, 1e-6, base + 8192, base + (1 << 16))
+    assert lib.qi4_w4g64_gate_up_silu_norm(ctypes.byref(big), 17, 64, 16, 16, None, 16, 16, None, 16, 64, None) == -3
+    bad_dt = lm.RmsNormPrologue(base, base + (1 << 16), 0, 1e-6, base + 8192, base + (1 << 17))
+    assert lib.qi4_w4g64_gate_up_silu_norm(ctypes.byref(bad_dt), 1, 64, 16, 16, None, 16, 16, None, 16, 64, None) == -2
+    misaligned = lm.RmsNormPrologue(base + 2, None, -1, 1e-6, base + 8192, base + (1 << 17))
+    assert lib.qi4_w4g64_linear_multi_norm(ctypes.byref(misaligned), 1, 64, 1, one, one, one, one, -1, one, ns,
+                                           None) == -4
