@@ -242,6 +242,25 @@ QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const voi
                                      void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
                                      void* stream);
 
+/* The same with a caller-owned workspace (`workspace_bytes` >= the size
+ * qi4_gqa_decode_attention_workspace returns, 16-byte aligned; NULL: the
+ * library's scratch pool), so that a captured graph holds only the kernels,
+ * and flags: QI4_ATTN_EARLY_CACHE_READ lets the kernel read lengths,
+ * positions and the past cache rows before it waits for the launch just
+ * before it (it still waits before reading q, k_new and v_new) - only for
+ * callers whose immediately preceding launches write none of them (a decode
+ * step whose attention follows the q/k/v projection). cos / sin must be
+ * 16-byte aligned. */
+#define QI4_ATTN_EARLY_CACHE_READ 1
+QI4_API size_t qi4_gqa_decode_attention_workspace(int64_t B, int64_t Hq, int64_t Hkv, int64_t cache_capacity);
+QI4_API int qi4_gqa_decode_attention_ex(const void* q, const void* k_new, const void* v_new, const void* cos,
+                                        const void* sin, const int32_t* positions, void* k_cache, void* v_cache,
+                                        int64_t cache_batch_stride, int64_t cache_head_stride,
+                                        int64_t cache_capacity, const int32_t* lengths, const uint8_t* key_mask,
+                                        int64_t mask_stride, void* out, int64_t B, int64_t Hq, int64_t Hkv,
+                                        int64_t head_dim, float scale, int flags, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
 /* Residual add + RMSNorm at a decoder block boundary (the reference's
  * DecoderLayer / RMSNorm, src/qwen_int4/model.py:31-42,151-159), in place on
  * the bf16 residual stream h [B, D]:
@@ -291,6 +310,12 @@ QI4_API int qi4_w4g64_gate_up_silu_norm(const qi4_rmsnorm_prologue* norm, int64_
  */
 QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
                                  int64_t* argmax, void* stream);
+
+/* The same with a caller-owned argmax workspace: `keys` holds 8 64-bit words
+ * that are zero on entry and left zero on return (the call's last kernel
+ * resets them), so a captured graph needs no allocation or memset around it. */
+QI4_API int qi4_bf16_gemv_argmax_ws(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
+                                    int64_t* argmax, uint64_t* keys, void* stream);
 
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),

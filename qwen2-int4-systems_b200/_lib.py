@@ -40,7 +40,11 @@ SIGNATURES = {
     "qi4_chain_destroy": [_p],
     "qi4_gqa_decode_attention": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i64,
                                  _i64, _i64, ctypes.c_float, _p],
+    "qi4_gqa_decode_attention_workspace": [_i64, _i64, _i64, _i64],
+    "qi4_gqa_decode_attention_ex": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i64, _p, _i64, _i64,
+                                    _i64, _i64, ctypes.c_float, _i, _p, _sz, _p],
     "qi4_bf16_gemv_argmax": [_p, _p, _i64, _i64, _i64, _p, _p, _p],
+    "qi4_bf16_gemv_argmax_ws": [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p],
     "qi4_add_rmsnorm": [_p, _p, _i, _p, _p, _i64, _i64, ctypes.c_float, _p],
     "qi4_w4g64_linear_multi_norm": [_p, _i64, _i64, _i, _p, _p, _p, _p, _i, _p, _p, _p],
     "qi4_w4g64_gate_up_silu_norm": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
@@ -48,7 +52,11 @@ SIGNATURES = {
     "qi4_version": [],
 }
 
+# Return types other than the int status.
+RESTYPES = {"qi4_gqa_decode_attention_workspace": ctypes.c_size_t}
+
 CHAIN_SWIGLU = 1
+ATTN_EARLY_CACHE_READ = 1
 
 
 class RmsNormPrologue(ctypes.Structure):
@@ -91,7 +99,7 @@ def load() -> ctypes.CDLL:
             for name, args in SIGNATURES.items():
                 fn = getattr(lib, name)
                 fn.argtypes = args
-                fn.restype = ctypes.c_int
+                fn.restype = RESTYPES.get(name, ctypes.c_int)
             _lib = lib
     return _lib
 

@@ -57,11 +57,12 @@ def b200_gqa_decode_attention(q, k_new, v_new, k_cache, v_cache, lengths, *, cos
             raise TypeError("decode attention takes bf16 CUDA tensors")
     if k_cache.stride(-1) != 1 or k_cache.stride(-2) != D or v_cache.stride() != k_cache.stride():
         raise ValueError("KV caches must be [B, Hkv, capacity, D] with contiguous rows and equal strides")
-    q, k_new, v_new = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    a16 = lambda t: t if t.data_ptr() % 16 == 0 else t.clone()  # noqa: E731  (the kernel copies 16-byte chunks)
+    q, k_new, v_new = a16(q.contiguous()), a16(k_new.contiguous()), a16(v_new.contiguous())
     if lengths.dtype != torch.int32 or not lengths.is_cuda:
         raise TypeError("lengths must be an int32 CUDA tensor")
     if cos is not None:
-        cos, sin = cos.contiguous(), sin.contiguous()
+        cos, sin = a16(cos.contiguous()), a16(sin.contiguous())
         if cos.dtype != torch.bfloat16 or sin.dtype != torch.bfloat16 or cos.shape[-1] != D:
             raise TypeError("cos / sin must be bf16 rows of head_dim")
     mask = None

@@ -20,8 +20,10 @@
 // split) and all G query heads of that KV head, so K and V are read once for
 // the group (no expansion). The split's keys and values are copied into
 // shared memory (asynchronous 16-byte copies, all in flight while the queries
-// are rotated), rows padded so that the reads below are conflict-free. 4
-// warps take 16 keys each, 8 at a time: lane (key kk = lane % 8, quarter
+// are rotated), rows padded so that the reads below are conflict-free.
+// Warps take 8 keys at a time (8 warps, one group each, for small grids,
+// whose duration is a warp's serial chain; 4 warps, two groups each,
+// otherwise): lane (key kk = lane % 8, quarter
 // dq = lane / 8) dots its 32 dims of the key with the G queries (held in
 // shared memory, FP32), a 2-step shuffle sums the quarters; per head an
 // online softmax (running max, rescaled sums) and P.V with lane = 4 output
@@ -42,7 +44,11 @@ namespace {
 constexpr int kD = 128;          // head dim
 constexpr int kMaxGroup = 8;     // query heads per KV head
 constexpr int kSplitKeys = 64;   // keys per CTA
-constexpr int kWarps = 4;
+// Warps per CTA: 8 (one 8-key group each per 64-key split) when the grid is
+// small - a batch-1 step runs ~20 CTAs, and a warp's serial chain of groups
+// is then the kernel's duration - else 4 (two groups each: less reduction
+// work and more CTAs resident per SM for large batches).
+constexpr int kWarpsSmallGrid = 8, kWarpsLargeGrid = 4;
 constexpr int kQPad = 36;        // floats per (head, quarter) row: 32 + 4 (bank spread)
 
 struct AttnArgs {
@@ -61,6 +67,7 @@ struct AttnArgs {
   float* partial;              // [B][Hkv][splits][G][kD + 2]
   int B, Hq, Hkv, G, cap, splits;
   float scale;
+  int early;                   // 1: lengths, positions and the past cache rows are read before the dependency wait
 };
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
@@ -81,12 +88,16 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
+template <int kWarps>
 __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs a) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   // Programmatic dependent launch: the next kernel may start its prologue;
-  // this one waits for its predecessor (the q/k/v projections) first.
+  // this one waits for its predecessor (the q/k/v projections) before it
+  // reads q / k_new / v_new - and, unless the caller vouched that lengths and
+  // the past cache rows are not written by the launches just before this one
+  // (`early`), before anything at all.
   pdl_launch_dependents();
-  pdl_wait();
+  if (!a.early) pdl_wait();
   const int L = a.lengths[b];  // past keys; the new one is key L
   const int nkeys = L + 1;
   const int k0 = split * kSplitKeys;
@@ -112,39 +123,51 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
     cp_async16(smem_addr_u(&kv_s[0][r][c * 16]), kbase + (int64_t)(k0 + r) * kD + c * 8);
     cp_async16(smem_addr_u(&kv_s[1][r][c * 16]), vbase + (int64_t)(k0 + r) * kD + c * 8);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-
-  // 2. Meanwhile: RoPE of the queries, and of the new key if it is in this split.
-  const __nv_bfloat16* cs = nullptr;
-  const __nv_bfloat16* sn = nullptr;
-  if (a.cos) {
+  // The RoPE row (a constant table, at positions[b]) travels with them.
+  const bool rope_on = a.cos != nullptr;
+  __shared__ __align__(16) __nv_bfloat16 cs_s[kD], sn_s[kD];    // cos / sin row
+  __shared__ __align__(16) __nv_bfloat16 qraw_s[kMaxGroup][kD];  // the G query heads, as given
+  __shared__ __align__(16) __nv_bfloat16 kn_s[kD], vn_s[kD];     // the new key / value
+  if (rope_on && tid < 32) {
     const int64_t row = a.positions ? a.positions[b] : b;
-    cs = a.cos + row * kD;
-    sn = a.sin + row * kD;
+    cp_async16(smem_addr_u((tid < 16 ? cs_s : sn_s) + (tid & 15) * 8),
+               (tid < 16 ? a.cos : a.sin) + row * kD + (tid & 15) * 8);
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  if (a.early) pdl_wait();  // the past rows stream in while the projections finish
+
+  // 2. The projections' outputs (one more round of copies): the G query heads
+  // and, in the split that holds key L, the new key and value.
+  const bool has_new = k0 <= L && L < k1;
+  for (int i = tid; i < G * 16; i += blockDim.x) {
+    const int h = i >> 4, c = i & 15;
+    cp_async16(smem_addr_u(&qraw_s[h][c * 8]), a.q + ((int64_t)b * a.Hq + kvh * G + h) * kD + c * 8);
+  }
+  if (has_new && tid < 32)
+    cp_async16(smem_addr_u((tid < 16 ? kn_s : vn_s) + (tid & 15) * 8),
+               (tid < 16 ? a.k_new : a.v_new) + ((int64_t)b * a.Hkv + kvh) * kD + (tid & 15) * 8);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // RoPE of the queries, and of the new key (staged as row L - k0 and
+  // appended to the cache), from shared memory.
   for (int i = tid; i < G * kD; i += blockDim.x) {
     const int h = i / kD, d = i - h * kD;
-    const __nv_bfloat16* qh = a.q + ((int64_t)b * a.Hq + kvh * G + h) * kD;
-    q_s[h][d >> 5][d & 31] = cs ? rope(qh, cs, sn, d) : bf(qh[d]);
+    q_s[h][d >> 5][d & 31] = rope_on ? rope(qraw_s[h], cs_s, sn_s, d) : bf(qraw_s[h][d]);
   }
-  const bool has_new = k0 <= L && L < k1;
   if (has_new) {
-    // The new key / value: staged as row L - k0, and appended to the cache.
-    const __nv_bfloat16* kn = a.k_new + ((int64_t)b * a.Hkv + kvh) * kD;
-    const __nv_bfloat16* vn = a.v_new + ((int64_t)b * a.Hkv + kvh) * kD;
     __nv_bfloat16* kc = a.k_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
     __nv_bfloat16* vc = a.v_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
     __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(&kv_s[0][L - k0][0]);
     __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(&kv_s[1][L - k0][0]);
     for (int d = tid; d < kD; d += blockDim.x) {
-      const __nv_bfloat16 kv = cs ? __float2bfloat16_rn(rope(kn, cs, sn, d)) : kn[d];
+      const __nv_bfloat16 kv = rope_on ? __float2bfloat16_rn(rope(kn_s, cs_s, sn_s, d)) : kn_s[d];
       ks[d] = kv;
-      vs[d] = vn[d];
+      vs[d] = vn_s[d];
       kc[d] = kv;
-      vc[d] = vn[d];
+      vc[d] = vn_s[d];
     }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   // 3. Keys 8 at a time per warp: lane (key kk = lane % 8, quarter dq = lane / 8).
@@ -313,8 +336,10 @@ int attention_splits(int cap) { return (cap + kSplitKeys - 1) / kSplitKeys; }
 cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_new, const void* cos, const void* sin,
                               const int32_t* positions, void* k_cache, void* v_cache, int64_t cb, int64_t ch,
                               const int32_t* lengths, const uint8_t* key_mask, int64_t mask_stride, void* out,
-                              float* partial, int B, int Hq, int Hkv, int cap, float scale, cudaStream_t stream) {
+                              float* partial, int B, int Hq, int Hkv, int cap, float scale, int early,
+                              cudaStream_t stream) {
   AttnArgs a;
+  a.early = early;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k_new = static_cast<const __nv_bfloat16*>(k_new);
   a.v_new = static_cast<const __nv_bfloat16*>(v_new);
@@ -341,11 +366,16 @@ cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_ne
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, Hkv, B);
-  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool small = (int64_t)a.splits * Hkv * B <= 2 * (int64_t)sms;
+  cfg.blockDim = dim3((small ? kWarpsSmallGrid : kWarpsLargeGrid) * 32, 1, 1);
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_decode_kernel, a);
+  cudaError_t e = small ? cudaLaunchKernelEx(&cfg, gqa_decode_kernel<kWarpsSmallGrid>, a)
+                        : cudaLaunchKernelEx(&cfg, gqa_decode_kernel<kWarpsLargeGrid>, a);
   if (e != cudaSuccess) return e;
   cfg.gridDim = dim3(Hq, B, 1);
   cfg.blockDim = dim3(kD, 1, 1);
@@ -368,14 +398,19 @@ int read_attention_error(cudaStream_t stream) {
 
 }  // namespace qi4
 
-extern "C" QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const void* v_new, const void* cos,
-                                                const void* sin, const int32_t* positions, void* k_cache,
-                                                void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
-                                                int64_t cache_capacity, const int32_t* lengths,
-                                                const uint8_t* key_mask, int64_t mask_stride, void* out, int64_t B,
-                                                int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
-                                                void* stream_ptr) {
-  using namespace qi4;
+namespace qi4 {
+namespace {
+
+size_t attention_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t cap) {
+  const int splits = attention_splits((int)std::min<int64_t>(cap, 1 << 24));
+  return (size_t)B * Hkv * splits * (Hq / Hkv) * (kD + 2) * sizeof(float);
+}
+
+int attention_impl(const void* q, const void* k_new, const void* v_new, const void* cos, const void* sin,
+                   const int32_t* positions, void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                   int64_t cache_head_stride, int64_t cache_capacity, const int32_t* lengths, const uint8_t* key_mask,
+                   int64_t mask_stride, void* out, int64_t B, int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
+                   int flags, void* workspace, size_t workspace_bytes, void* stream_ptr) {
   clear_error();
   if (!q || !k_new || !v_new || !k_cache || !v_cache || !lengths || !out || (!cos != !sin)) {
     set_error("q, k_new, v_new, the caches, lengths and out must be non-null (cos and sin both or neither)");
@@ -390,17 +425,25 @@ extern "C" QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new
               kMaxGroup, (long long)head_dim, (long long)Hq, (long long)Hkv);
     return QI4_ERR_SHAPE;
   }
+  if (flags & ~QI4_ATTN_EARLY_CACHE_READ) {
+    set_error("unknown decode attention flags 0x%x", flags);
+    return QI4_ERR_ARGUMENT;
+  }
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al16(k_cache) || !al16(v_cache) || cache_batch_stride % 8 || cache_head_stride % 8 || !al16(q) ||
-      !al16(k_new) || !al16(v_new)) {
-    set_error("caches and q/k/v must be 16-byte aligned with strides a multiple of 8 elements");
+      !al16(k_new) || !al16(v_new) || (cos && (!al16(cos) || !al16(sin)))) {
+    set_error("caches, q/k/v and cos/sin must be 16-byte aligned with strides a multiple of 8 elements");
     return QI4_ERR_ALIGNMENT;
   }
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const int splits = attention_splits((int)std::min<int64_t>(cache_capacity, 1 << 24));
-  void* partial = nullptr;
-  const size_t bytes = (size_t)B * Hkv * splits * (Hq / Hkv) * (kD + 2) * sizeof(float);
-  if (scratch_alloc(&partial, bytes, stream) != cudaSuccess) {
+  const size_t bytes = attention_workspace_bytes(B, Hq, Hkv, cache_capacity);
+  void* partial = workspace;
+  if (workspace) {
+    if (workspace_bytes < bytes || !al16(workspace)) {
+      set_error("decode attention workspace needs %zu bytes, 16-byte aligned (got %zu)", bytes, workspace_bytes);
+      return QI4_ERR_ARGUMENT;
+    }
+  } else if (scratch_alloc(&partial, bytes, stream) != cudaSuccess) {
     cudaGetLastError();
     set_error("cannot allocate %zu bytes of attention scratch", bytes);
     return QI4_ERR_LAUNCH;
@@ -408,12 +451,47 @@ extern "C" QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new
   const cudaError_t e = launch_gqa_decode(q, k_new, v_new, cos, sin, positions, k_cache, v_cache, cache_batch_stride,
                                           cache_head_stride, lengths, key_mask, mask_stride, out,
                                           static_cast<float*>(partial), (int)B, (int)Hq, (int)Hkv,
-                                          (int)cache_capacity, scale, stream);
-  scratch_free(partial, stream);
+                                          (int)cache_capacity, scale, (flags & QI4_ATTN_EARLY_CACHE_READ) ? 1 : 0,
+                                          stream);
+  if (!workspace) scratch_free(partial, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("decode attention launch failed: %s", cudaGetErrorString(e));
     return QI4_ERR_LAUNCH;
   }
   return QI4_OK;
+}
+
+}  // namespace
+}  // namespace qi4
+
+extern "C" QI4_API int qi4_gqa_decode_attention(const void* q, const void* k_new, const void* v_new, const void* cos,
+                                                const void* sin, const int32_t* positions, void* k_cache,
+                                                void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                                                int64_t cache_capacity, const int32_t* lengths,
+                                                const uint8_t* key_mask, int64_t mask_stride, void* out, int64_t B,
+                                                int64_t Hq, int64_t Hkv, int64_t head_dim, float scale,
+                                                void* stream_ptr) {
+  return qi4::attention_impl(q, k_new, v_new, cos, sin, positions, k_cache, v_cache, cache_batch_stride,
+                             cache_head_stride, cache_capacity, lengths, key_mask, mask_stride, out, B, Hq, Hkv,
+                             head_dim, scale, 0, nullptr, 0, stream_ptr);
+}
+
+extern "C" QI4_API size_t qi4_gqa_decode_attention_workspace(int64_t B, int64_t Hq, int64_t Hkv,
+                                                             int64_t cache_capacity) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || cache_capacity <= 0 || Hq % Hkv) return 0;
+  return qi4::attention_workspace_bytes(B, Hq, Hkv, cache_capacity);
+}
+
+extern "C" QI4_API int qi4_gqa_decode_attention_ex(const void* q, const void* k_new, const void* v_new,
+                                                   const void* cos, const void* sin, const int32_t* positions,
+                                                   void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                                                   int64_t cache_head_stride, int64_t cache_capacity,
+                                                   const int32_t* lengths, const uint8_t* key_mask,
+                                                   int64_t mask_stride, void* out, int64_t B, int64_t Hq, int64_t Hkv,
+                                                   int64_t head_dim, float scale, int flags, void* workspace,
+                                                   size_t workspace_bytes, void* stream_ptr) {
+  return qi4::attention_impl(q, k_new, v_new, cos, sin, positions, k_cache, v_cache, cache_batch_stride,
+                             cache_head_stride, cache_capacity, lengths, key_mask, mask_stride, out, B, Hq, Hkv,
+                             head_dim, scale, flags, workspace, workspace_bytes, stream_ptr);
 }

@@ -42,6 +42,8 @@ __global__ void __launch_bounds__(kThreads) gemv_argmax_kernel(const __nv_bfloat
                                                                int64_t rows_per_cta) {
   extern __shared__ uint4 xs_raw[];  // [M][K] bf16
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_launch_dependents();
+  pdl_wait();  // x is the previous kernel's output
   for (int i = tid; i < M * K / 8; i += kThreads) xs_raw[i] = reinterpret_cast<const uint4*>(x)[i];
   __syncthreads();
   const uint32_t xs = (uint32_t)__cvta_generic_to_shared(xs_raw);
@@ -140,9 +142,28 @@ __global__ void __launch_bounds__(kThreads) gemv_argmax_kernel(const __nv_bfloat
   }
 }
 
-__global__ void argmax_finalize_kernel(const unsigned long long* keys, int64_t* out, int M) {
+// Keys -> indices; the keys are left zero again, ready for the next call.
+__global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t* out, int M) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int t = threadIdx.x;
-  if (t < M) out[t] = keys[t] ? (int64_t)(0xFFFFFFFFull - (keys[t] & 0xFFFFFFFFull)) : 0;
+  if (t < M) {
+    out[t] = keys[t] ? (int64_t)(0xFFFFFFFFull - (keys[t] & 0xFFFFFFFFull)) : 0;
+    keys[t] = 0;
+  }
+}
+
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr) {
+  attr->id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr->val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
 }
 
 template <int M>
@@ -154,19 +175,22 @@ cudaError_t launch_m(const void* w, const void* x, int64_t N, int K, void* logit
                                                (int)smem);
     if (e != cudaSuccess) return e;
   }
-  gemv_argmax_kernel<M><<<grid, kThreads, smem, stream>>>(static_cast<const __nv_bfloat16*>(w),
-                                                          static_cast<const __nv_bfloat16*>(x), N, K,
-                                                          static_cast<__nv_bfloat16*>(logits), keys, rows_per_cta);
-  return cudaGetLastError();
+  cudaLaunchAttribute attr;
+  const cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kThreads), smem, stream, &attr);
+  return cudaLaunchKernelEx(&cfg, gemv_argmax_kernel<M>, static_cast<const __nv_bfloat16*>(w),
+                            static_cast<const __nv_bfloat16*>(x), N, K, static_cast<__nv_bfloat16*>(logits), keys,
+                            rows_per_cta);
 }
 
 }  // namespace
 
 }  // namespace qi4
 
-extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N,
-                                            void* logits, int64_t* argmax, void* stream_ptr) {
-  using namespace qi4;
+namespace qi4 {
+namespace {
+
+int lm_head_impl(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits, int64_t* argmax,
+                 unsigned long long* keys_ws, void* stream_ptr) {
   clear_error();
   if (!weight || !x || (!logits && !argmax)) {
     set_error("weight and x must be non-null, and at least one of logits / argmax");
@@ -185,8 +209,8 @@ extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, i
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  void* keys = nullptr;
-  if (argmax) {
+  void* keys = keys_ws;
+  if (argmax && !keys) {
     if (scratch_alloc(&keys, kMaxTok * sizeof(unsigned long long), stream) != cudaSuccess) {
       cudaGetLastError();
       set_error("cannot allocate the argmax scratch");
@@ -196,7 +220,7 @@ extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, i
   }
   const int grid = sms * 4;
   const int64_t rows_per_cta = ((N + grid - 1) / grid + kRows - 1) / kRows * kRows;
-  auto k = static_cast<unsigned long long*>(keys);
+  auto k = argmax ? static_cast<unsigned long long*>(keys) : nullptr;
   cudaError_t e;
   switch (M) {
     case 1: e = launch_m<1>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
@@ -209,14 +233,34 @@ extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, i
     default: e = launch_m<8>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;  // M == 8
   }
   if (e == cudaSuccess && argmax) {
-    argmax_finalize_kernel<<<1, 32, 0, stream>>>(k, argmax, (int)M);
-    e = cudaGetLastError();
+    cudaLaunchAttribute attr;
+    const cudaLaunchConfig_t cfg = pdl_config(dim3(1), dim3(32), 0, stream, &attr);
+    e = cudaLaunchKernelEx(&cfg, argmax_finalize_kernel, k, argmax, (int)M);
   }
-  if (keys) scratch_free(keys, stream);
+  if (keys && !keys_ws) scratch_free(keys, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();
     set_error("lm_head GEMV launch failed: %s", cudaGetErrorString(e));
     return QI4_ERR_LAUNCH;
   }
   return QI4_OK;
+}
+
+}  // namespace
+}  // namespace qi4
+
+extern "C" QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, int64_t K, int64_t N,
+                                            void* logits, int64_t* argmax, void* stream_ptr) {
+  return qi4::lm_head_impl(weight, x, M, K, N, logits, argmax, nullptr, stream_ptr);
+}
+
+extern "C" QI4_API int qi4_bf16_gemv_argmax_ws(const void* weight, const void* x, int64_t M, int64_t K, int64_t N,
+                                               void* logits, int64_t* argmax, uint64_t* keys, void* stream_ptr) {
+  using namespace qi4;
+  if (argmax && (!keys || (reinterpret_cast<uintptr_t>(keys) & 7))) {
+    clear_error();
+    set_error("the argmax workspace must be 8 zeroed, 8-byte aligned 64-bit words");
+    return QI4_ERR_ARGUMENT;
+  }
+  return lm_head_impl(weight, x, M, K, N, logits, argmax, reinterpret_cast<unsigned long long*>(keys), stream_ptr);
 }

@@ -111,6 +111,11 @@ class DecodeEngine:
             pos = torch.arange(max_len, device=dev).view(1, -1)
             cos, sin = model.model.rotary_emb(pos, torch.bfloat16)
         self.cos, self.sin = cos[0].contiguous(), sin[0].contiguous()
+        # Caller-owned workspaces: the captured step holds only kernel nodes,
+        # so programmatic dependent launch links every kernel to the next.
+        ws = self.lib.qi4_gqa_decode_attention_workspace(B, self.Hq, self.Hkv, max_len)
+        self.attn_ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.lm_keys = torch.zeros(8, dtype=torch.int64, device=dev)
         self.graph = None
         self.stream = torch.cuda.Stream(device=dev)
 
@@ -155,11 +160,14 @@ class DecodeEngine:
                 rc = L.qi4_w4g64_linear_multi(self.x.data_ptr(), BF16, B, self.D, *mats)
             _lib.check(rc, "qi4_w4g64_linear_multi")
             kc, vc = self.kcache[li], self.vcache[li]
-            rc = L.qi4_gqa_decode_attention(
+            # Early cache reads: within a step nothing writes the caches or
+            # lengths before the attention of a layer but that attention.
+            rc = L.qi4_gqa_decode_attention_ex(
                 self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
                 self.positions.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.stride(0), kc.stride(1), self.max_len,
                 self.lengths.data_ptr(), self.key_mask.data_ptr(), self.key_mask.stride(0), self.attn.data_ptr(), B,
-                self.Hq, self.Hkv, self.hd, float(self.hd ** -0.5), self._s)
+                self.Hq, self.Hkv, self.hd, float(self.hd ** -0.5), _lib.ATTN_EARLY_CACHE_READ,
+                self.attn_ws.data_ptr(), self.attn_ws.numel(), self._s)
             _lib.check(rc, "qi4_gqa_decode_attention")
             self._linear(lay["o"], self.attn, BF16, self.o)
             g, u = lay["gate"], lay["up"]
@@ -176,8 +184,9 @@ class DecodeEngine:
             delta, ddt = self.y, F32
         self._norm(self.hbuf[self._cur], delta, ddt, self.w_final)
         if B <= 8:
-            rc = L.qi4_bf16_gemv_argmax(self.lm_weight.data_ptr(), self.x.data_ptr(), B, self.D,
-                                        self.lm_weight.shape[0], None, self.next.data_ptr(), self._s)
+            rc = L.qi4_bf16_gemv_argmax_ws(self.lm_weight.data_ptr(), self.x.data_ptr(), B, self.D,
+                                           self.lm_weight.shape[0], None, self.next.data_ptr(),
+                                           self.lm_keys.data_ptr(), self._s)
             _lib.check(rc, "qi4_bf16_gemv_argmax")
         else:
             torch.argmax(torch.nn.functional.linear(self.x, self.lm_weight), dim=-1, out=self.next)

@@ -10,6 +10,7 @@ forward and with the unpatched decode, and a forked cache keeps both
 continuations apart.
 """
 
+import ctypes
 import importlib
 
 import pytest
@@ -140,3 +141,38 @@ def test_forked_cache_continuations_stay_apart(b200, cuda_device):
         assert not torch.equal(ca[0][0], cb[0][0])
     finally:
         q2.register_with_reference(ref_name, fast_attention=False)
+
+
+def test_workspace_and_early_cache_read_give_the_same_result(b200, cuda_device):
+    """qi4_gqa_decode_attention_ex with a caller workspace (and the early cache
+    read a decode step may use) equals the plain call bit for bit; a workspace
+    that is too small is rejected before any launch."""
+    lm = importlib.import_module(b200.__name__ + "._lib")
+    lib = lm.load()
+    g = torch.Generator(device="cpu").manual_seed(12)
+    B, L, Hq, Hkv, D, cap = 3, 200, 12, 2, 128, 256
+    bf = dict(dtype=torch.bfloat16, device=cuda_device)
+    q = torch.randn(B, Hq, D, generator=g).to(**bf)
+    kn, vn = torch.randn(B, Hkv, D, generator=g).to(**bf), torch.randn(B, Hkv, D, generator=g).to(**bf)
+    kc0, vc0 = torch.randn(B, Hkv, cap, D, generator=g).to(**bf), torch.randn(B, Hkv, cap, D, generator=g).to(**bf)
+    lengths = torch.tensor([L, L - 77, 5], dtype=torch.int32, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for mode in ("plain", "ws", "ws_early"):
+        kc, vc = kc0.clone(), vc0.clone()
+        out = torch.empty(B, Hq * D, **bf)
+        args = (q.data_ptr(), kn.data_ptr(), vn.data_ptr(), None, None, None, kc.data_ptr(), vc.data_ptr(),
+                kc.stride(0), kc.stride(1), cap, lengths.data_ptr(), None, 0, out.data_ptr(), B, Hq, Hkv, D,
+                ctypes.c_float(D ** -0.5))
+        if mode == "plain":
+            assert lib.qi4_gqa_decode_attention(*args, s) == 0
+        else:
+            n = lib.qi4_gqa_decode_attention_workspace(B, Hq, Hkv, cap)
+            ws = torch.empty(n, dtype=torch.uint8, device=cuda_device)
+            flags = lm.ATTN_EARLY_CACHE_READ if mode == "ws_early" else 0
+            assert lib.qi4_gqa_decode_attention_ex(*args, flags, ws.data_ptr(), n - 16, s) == -1  # too small
+            assert lib.qi4_gqa_decode_attention_ex(*args, flags, ws.data_ptr(), n, s) == 0
+        torch.cuda.synchronize()
+        outs.append((out, kc, vc))
+    for out, kc, vc in outs[1:]:
+        assert torch.equal(out, outs[0][0]) and torch.equal(kc, outs[0][1]) and torch.equal(vc, outs[0][2])

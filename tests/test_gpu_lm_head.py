@@ -41,3 +41,26 @@ def test_lm_head_argmax_only_skips_logits_and_breaks_ties_to_first(b200, cuda_de
     logits, arg = b200.b200_lm_head(x, w, return_logits=False)
     assert logits is None
     assert arg.tolist() == [17, 17]
+
+
+def test_argmax_with_caller_workspace_leaves_it_zero(b200, cuda_device):
+    """qi4_bf16_gemv_argmax_ws gives the plain call's tokens, and its 8-word
+    workspace is zero again after every call (so repeated calls need no
+    memset)."""
+    import ctypes
+    from importlib import import_module
+
+    lib = import_module(b200.__name__ + "._lib").load()
+    g = torch.Generator().manual_seed(3)
+    w = (torch.randn(151936, 1536, generator=g) * 0.02).to(torch.bfloat16).to(cuda_device)
+    keys = torch.zeros(8, dtype=torch.int64, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    for m in (1, 3, 8):
+        x = torch.randn(m, 1536, generator=g).to(torch.bfloat16).to(cuda_device)
+        a, b = (torch.empty(m, dtype=torch.int64, device=cuda_device) for _ in range(2))
+        assert lib.qi4_bf16_gemv_argmax(w.data_ptr(), x.data_ptr(), m, 1536, 151936, None, a.data_ptr(), s) == 0
+        assert lib.qi4_bf16_gemv_argmax_ws(w.data_ptr(), x.data_ptr(), m, 1536, 151936, None, b.data_ptr(),
+                                           keys.data_ptr(), s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(a, b) and int(keys.abs().sum()) == 0
+    assert lib.qi4_bf16_gemv_argmax_ws(w.data_ptr(), x.data_ptr(), 1, 1536, 151936, None, b.data_ptr(), None, s) == -1
