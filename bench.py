@@ -31,7 +31,9 @@ checkpoint is used).
             backend
   split_prefill_mlp = the M = 4096 MLP unsplit on one GPU (N = 1) or split over
             the ranks (column / column_row), with an output check
-  roofline, cpu_baseline, clocks: see the JSON keys.
+  roofline = the step's largest kernel, the fused gate/up + SwiGLU GEMV, over a
+            28-launch chain (the gate-only GEMV beside it)
+  cpu_baseline, clocks: see the JSON keys.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 Multi-GPU (torchrun): independent replicas, one per rank, weak scaling.
@@ -327,6 +329,34 @@ class GroupedChain:
             rc = self.lib.qi4_w4g64_linear_multi(x.data_ptr(), BF16, self.m, k, c, qw, sc, z, b, bd, o, ns, stream)
             if rc:
                 raise RuntimeError(f"grouped launch failed: {rc}")
+
+    def graph(self):
+        return capture(self.launch)
+
+
+class SwigluChain:
+    """The fused gate/up + SwiGLU GEMV (qi4_w4g64_gate_up_silu) of every layer
+    at M = 1, chained (independent bf16 inputs, FP32 outputs): the largest
+    kernel of the headline step."""
+
+    def __init__(self, lib, layers: list[list[dict]], device, gen: torch.Generator):
+        self.lib, self.items = lib, []
+        for layer in layers:
+            g, u = layer[4], layer[5]
+            x = torch.randn(1, 1536, device=device, generator=gen).to(torch.bfloat16)
+            out = torch.empty(1, 8960, device=device, dtype=torch.float32)
+            self.items.append((x, g, u, out))
+        self.bytes_per_launch = 2 * weight_bytes(8960, 1536) + 1536 * 2 + 8960 * 4
+
+    def launch(self):
+        stream = torch.cuda.current_stream().cuda_stream
+        for x, g, u, out in self.items:
+            rc = self.lib.qi4_w4g64_gate_up_silu(x.data_ptr(), BF16, 1, 1536, g["qweight"].data_ptr(),
+                                                 g["scales"].data_ptr(), g["zeros"].data_ptr(),
+                                                 u["qweight"].data_ptr(), u["scales"].data_ptr(),
+                                                 u["zeros"].data_ptr(), out.data_ptr(), 8960, stream)
+            if rc:
+                raise RuntimeError(f"gate/up launch failed: {rc}")
 
     def graph(self):
         return capture(self.launch)
@@ -762,14 +792,66 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
 
 
 def profile_case(kind: str) -> None:
-    """Small, ncu-sized run of the dominant kernel (see --profile-case)."""
+    """Small, ncu-sized run of one kernel (see --profile-case)."""
     device = torch.device("cuda", 0)
     lib = importlib.import_module(PACKAGE + "._lib").load()
     gen = torch.Generator(device=device).manual_seed(0)
+    if kind == "attention":
+        # Config 4's decode attention: batch 64, 12 / 2 heads, 1024 past keys,
+        # two layers' caches (2 x 84 MB, more than L2) used alternately.
+        B, Hq, Hkv, D, cap, L = 64, 12, 2, 128, 1281, 1024
+        bf = dict(dtype=torch.bfloat16, device=device)
+        caches = [(torch.randn(B, Hkv, cap, D, generator=gen, device=device).to(torch.bfloat16),
+                   torch.randn(B, Hkv, cap, D, generator=gen, device=device).to(torch.bfloat16)) for _ in range(2)]
+        q = torch.randn(B, Hq, D, generator=gen, device=device).to(torch.bfloat16)
+        kv = torch.randn(B, Hkv, D, generator=gen, device=device).to(torch.bfloat16)
+        lengths = torch.full((B,), L, dtype=torch.int32, device=device)
+        out = torch.empty(B, Hq * D, **bf)
+        n = lib.qi4_gqa_decode_attention_workspace(B, Hq, Hkv, cap)
+        ws = torch.zeros(n, dtype=torch.uint8, device=device)
+        for i in range(4):
+            kc, vc = caches[i % 2]
+            rc = lib.qi4_gqa_decode_attention_ex(
+                q.data_ptr(), kv.data_ptr(), kv.data_ptr(), None, None, None, kc.data_ptr(), vc.data_ptr(),
+                kc.stride(0), kc.stride(1), cap, lengths.data_ptr(), None, 0, out.data_ptr(), B, Hq, Hkv, D,
+                ctypes.c_float(D ** -0.5), 0, ws.data_ptr(), n, torch.cuda.current_stream().cuda_stream)
+            if rc:
+                raise RuntimeError(f"attention launch failed: {rc}")
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": kind, "launches": 4, "kv_bytes_per_launch": 2 * B * Hkv * (L + 1) * D * 2}))
+        return
+    if kind == "lm_head":
+        # The tied lm_head at batch 1: 151936 x 1536 bf16 (467 MB) per launch.
+        w = (torch.randn(151936, 1536, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+        x = torch.randn(1, 1536, generator=gen, device=device).to(torch.bfloat16)
+        arg = torch.empty(1, dtype=torch.int64, device=device)
+        keys = torch.zeros(8, dtype=torch.int64, device=device)
+        for _ in range(3):
+            rc = lib.qi4_bf16_gemv_argmax_ws(w.data_ptr(), x.data_ptr(), 1, 1536, 151936, None, arg.data_ptr(),
+                                             keys.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            if rc:
+                raise RuntimeError(f"lm_head launch failed: {rc}")
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": kind, "launches": 3, "weight_bytes": w.numel() * 2}))
+        return
     ents = []
     for _ in range(8):
         qw, sc, z = quantize_symmetric_rtn_gpu(8960, 1536, gen, device)
         ents.append({"name": "gate", "k": 1536, "n": 8960, "qweight": qw, "scales": sc, "zeros": z, "bias": None})
+    if kind == "swiglu":
+        x = torch.randn(1, 1536, generator=gen, device=device).to(torch.bfloat16)
+        out = torch.empty(1, 8960, dtype=torch.float32, device=device)
+        for i in range(3):
+            g, u = ents[2 * i], ents[2 * i + 1]
+            rc = lib.qi4_w4g64_gate_up_silu(x.data_ptr(), BF16, 1, 1536, g["qweight"].data_ptr(),
+                                            g["scales"].data_ptr(), g["zeros"].data_ptr(), u["qweight"].data_ptr(),
+                                            u["scales"].data_ptr(), u["zeros"].data_ptr(), out.data_ptr(), 8960,
+                                            torch.cuda.current_stream().cuda_stream)
+            if rc:
+                raise RuntimeError(f"gate/up launch failed: {rc}")
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": kind, "launches": 3, "m": 1}))
+        return
     m, algo = (1, 1) if kind == "gemv" else (2048, 2)
     chain = Chain(lib, ents if kind == "gemv" else ents[:2], m, device, gen, algo=algo)
     for _ in range(3):
@@ -798,9 +880,12 @@ def main() -> None:
     parser.add_argument("--no-configs", action="store_true",
                         help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, "
                              "AWQ down, batch-64 linears)")
-    parser.add_argument("--profile-case", choices=["gemv", "gemm"],
+    parser.add_argument("--profile-case", choices=["gemv", "swiglu", "gemm", "attention", "lm_head"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
-                             "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv) or M=2048 (gemm)")
+                             "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv; swiglu: gate/up pairs "
+                             "fused) or M=2048 (gemm); "
+                             "4 decode-attention launches at batch 64 over 1024 keys (attention); 3 lm_head "
+                             "GEMV + argmax launches at batch 1 (lm_head)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
@@ -859,6 +944,10 @@ def main() -> None:
         t = time_graph(chain.graph(), reps=20, warmup=3)
         per_shape[name] = {"m": 1, "us_per_launch": t * 1e3 / LAYERS, "GBps": chain.bytes() / (t / 1e3) / 1e9}
     gate = per_shape["gate"]
+    sw = SwigluChain(lib, layers, device, gen)
+    t = time_graph(sw.graph(), reps=20, warmup=3)
+    swiglu = {"m": 1, "us_per_launch": t * 1e3 / LAYERS, "GBps": sw.bytes_per_launch * LAYERS / (t / 1e3) / 1e9,
+              "algorithmic_bytes_per_launch": sw.bytes_per_launch}
     variants = step_variants(lib, layers, device, gen, dist)
 
     peaks_path = ROOT / "MEASURED_PEAKS.json"
@@ -868,11 +957,18 @@ def main() -> None:
         tensor_peak = float(peaks.get("bf16_tflops", 1590.0))
     else:
         hbm_peak, peak_src, tensor_peak = 6650.0, "fallback", 1590.0
-    traffic = load_traffic().get("gemv_gate_m1_bytes_per_launch")
-    roofline = {"bound": "hbm", "kernel": "gemv_mma_kernel (gate 1536->8960, M=1)",
-                "achieved": gate["GBps"], "peak": hbm_peak, "unit": "GB/s",
-                "frac": gate["GBps"] / hbm_peak, "peak_source": peak_src,
-                "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False),
+    traffic = load_traffic()
+    roofline = {"bound": "hbm",
+                "kernel": "gemv_mma_kernel, fused gate/up + SwiGLU (2 x 1536->8960, M=1): the largest kernel "
+                          "of the step, 28 launches chained",
+                "achieved": swiglu["GBps"], "peak": hbm_peak, "unit": "GB/s",
+                "frac": swiglu["GBps"] / hbm_peak, "peak_source": peak_src,
+                "traffic": traffic.get("gemv_swiglu_m1_bytes_per_launch"),
+                "algorithmic_bytes_per_launch": sw.bytes_per_launch,
+                "gate_only": {"kernel": "gemv_mma_kernel (gate 1536->8960, M=1)", "achieved": gate["GBps"],
+                              "frac": gate["GBps"] / hbm_peak,
+                              "traffic": traffic.get("gemv_gate_m1_bytes_per_launch"),
+                              "algorithmic_bytes_per_launch": alg_bytes(1, 8960, 1536, False)},
                 "step_frac": step.nbytes / (ms_per_step / 1e3) / 1e9 / hbm_peak}
 
     configs = config_sweep(lib, layers, device, gen, tensor_peak) if not args.no_configs and world == 1 else None
@@ -911,7 +1007,8 @@ def main() -> None:
                    "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (655 MB packed weights per step); no flush"},
         "gpu_launches": 4 * LAYERS * args.steps,
-        "roofline": roofline, "per_shape_m1": per_shape, "decode_step_variants": variants,
+        "roofline": roofline, "per_shape_m1": per_shape, "gate_up_silu_m1": swiglu,
+        "decode_step_variants": variants,
         "gemm_m2048": gemm, "configs": configs, "serving": serving, "qwen2_decode": decode,
         "split_prefill_mlp": split, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary(),
     }))
