@@ -487,7 +487,7 @@ __device__ __forceinline__ void mma_group(float (&acc)[NT][4], const uint32_t* a
 template <int XT, int NT, int WARPS, int PRE>
 constexpr int kMinBlocks = WARPS == 16 ? 2 : (WARPS == 8 && NT == 1 && PRE == 0 && XT != QI4_DTYPE_F32) ? 4 : 1;
 
-template <int XT, int NT, int WARPS, int PRE, bool SW = false>
+template <int XT, int NT, int WARPS, int PRE, bool SW = false, bool NORM = false>
 __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) gemv_mma_kernel(const __grid_constant__ CUtensorMap wmap0, const __grid_constant__ CUtensorMap wmap1,
                 const __grid_constant__ CUtensorMap wmap2, const Args a) {
   // PRE > 0: every warp has at most PRE groups, expanded into registers
@@ -501,7 +501,9 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
   // Offset from the shared array itself (not an integer round trip), so that
   // every pointer derived from it stays in the shared address space.
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-  __shared__ float norm_rs[16];  // per-token RMSNorm factors of a fused norm prologue (M <= 16)
+  // NORM: x is formed from the residual stream while staging (a compile-time
+  // variant, so that the plain kernels keep their register budget).
+  __shared__ float norm_rs[NORM ? 16 : 1];  // per-token RMSNorm factors (M <= 16)
   constexpr int kWarpsLog2 = WARPS == 32 ? 5 : WARPS == 16 ? 4 : WARPS == 8 ? 3 : WARPS == 4 ? 2 : WARPS == 2 ? 1 : 0;
   static_assert((1 << kWarpsLog2) == WARPS, "warps per CTA must be a power of two");
   const int R = a.rows;
@@ -611,7 +613,7 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
       }
     }
     wait_prerequisites(tid);  // activations come from the previous kernel
-    if (XT == QI4_DTYPE_BF16 && a.has_norm)
+    if constexpr (NORM)
       stage_x_norm(a, xs, xstride, g0, gs, tid, kThr, norm_rs);
     else
       stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
@@ -621,7 +623,7 @@ __global__ void __launch_bounds__(WARPS * 32, kMinBlocks<XT, NT, WARPS, PRE>) ge
       if (gb + j < ge) mma_group<XT, NT>(acc, fa[j], fa[j] + 8, fs[j][0], fs[j][1], gb + j, x_row, gs);
   } else {
     wait_prerequisites(tid);  // activations come from the previous kernel
-    if (XT == QI4_DTYPE_BF16 && a.has_norm)
+    if constexpr (NORM)
       stage_x_norm(a, xs, xstride, g0, gs, tid, kThr, norm_rs);
     else
       stage_x<XT, PRE == 0>(a, xs, xstride, g0, gs, tid, kThr);
@@ -759,9 +761,9 @@ size_t smem_bytes(int R, int warps, int bps, int NT, int M, bool f32, int copy_l
   return 1024 + (size_t)alloc_boxes(bps, copy_log2) * R * kBoxBytes + table + red + xs + (size_t)bps * 8;
 }
 
-template <int XT, int NT, int WARPS, int PRE, bool SW = false>
+template <int XT, int NT, int WARPS, int PRE, bool SW = false, bool NORM = false>
 cudaError_t launch_t(const CUtensorMap* maps, const Args& a, int ksplit, cudaStream_t stream, bool pdl) {
-  auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE, SW>;
+  auto kernel = gemv_mma_kernel<XT, NT, WARPS, PRE, SW, NORM>;
   static unsigned long long configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -812,6 +814,21 @@ cudaError_t launch_w(const CUtensorMap* map, const Args& a, int warps, int kspli
 template <int XT>
 cudaError_t launch_x(const CUtensorMap* map, const Args& a, int nt, int warps, int ksplit, int pre,
                      cudaStream_t s, bool pdl) {
+  if (a.has_norm) {  // the fused block boundary: bf16, decode plans of 8 or 16 warps
+    // (with pre-wait expansion where the plan has it: 137 registers, one CTA
+    // per SM, still measured faster in the decode step than without it)
+    if constexpr (XT == QI4_DTYPE_BF16) {
+      if (warps == 8)
+        return nt <= 1 ? (pre ? launch_t<XT, 1, 8, kPreGroups, false, true>(map, a, ksplit, s, pdl)
+                              : launch_t<XT, 1, 8, 0, false, true>(map, a, ksplit, s, pdl))
+                       : (pre ? launch_t<XT, 2, 8, kPreGroups, false, true>(map, a, ksplit, s, pdl)
+                              : launch_t<XT, 2, 8, 0, false, true>(map, a, ksplit, s, pdl));
+      if (warps == 16)
+        return nt <= 1 ? launch_t<XT, 1, 16, 0, false, true>(map, a, ksplit, s, pdl)
+                       : launch_t<XT, 2, 16, 0, false, true>(map, a, ksplit, s, pdl);
+    }
+    return cudaErrorInvalidValue;
+  }
   return nt <= 1 ? launch_w<XT, 1>(map, a, warps, ksplit, pre, s, pdl)
                  : launch_w<XT, 2>(map, a, warps, ksplit, pre, s, pdl);
 }
@@ -955,6 +972,12 @@ namespace {
 
 template <int XT>
 cudaError_t launch_swiglu_x(const CUtensorMap* maps, const Args& a, int nt, cudaStream_t s, bool pdl) {
+  if (a.has_norm) {
+    if constexpr (XT == QI4_DTYPE_BF16)
+      return nt <= 1 ? launch_t<XT, 1, 8, 0, true, true>(maps, a, 1, s, pdl)
+                     : launch_t<XT, 2, 8, 0, true, true>(maps, a, 1, s, pdl);
+    return cudaErrorInvalidValue;
+  }
   return nt <= 1 ? launch_t<XT, 1, 8, 0, true>(maps, a, 1, s, pdl) : launch_t<XT, 2, 8, 0, true>(maps, a, 1, s, pdl);
 }
 
