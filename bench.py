@@ -978,14 +978,20 @@ def main() -> None:
     e2e = e2e_section(pkg, step, device, e2e_steps, dist)
     e2e = {"value": step.nbytes * world / (e2e["ms_per_step"] / 1e3) / 1e9, "unit": UNIT, **e2e}
 
-    split = split_prefill(device, dist, world)
+    try:
+        split = split_prefill(device, dist, world)
+    except Exception as exc:  # recorded, not fatal: the headline line is printed either way
+        split = {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
     step_bytes = step.nbytes
     del layers, step, step_graph
     torch.cuda.empty_cache()
     serving = decode = None
     if not args.no_model:
-        serving = serving_section(device, dist, world, full=world == 1)
+        try:
+            serving = serving_section(device, dist, world, full=world == 1)
+        except Exception as exc:
+            serving = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         if world == 1:
             decode = reference_harness_decode(device)
 
