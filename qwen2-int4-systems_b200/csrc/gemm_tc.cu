@@ -206,14 +206,28 @@ __host__ __device__ constexpr uint32_t make_idesc(int ab_bf16, int bn) {
 }
 
 // 8 codes (one packed word) -> 8 dequantised values packed as 4 x bf16x2/f16x2.
+// (a * s + c, b * s + c) with one packed FP32 FMA (sm_100a f32x2: each lane
+// rounded once, as two fmaf would be).
+__device__ __forceinline__ void fma2(float a, float b, float s, float c, float& ra, float& rb) {
+  asm("{\n\t.reg .b64 x, m, d, r;\n\t"
+      "mov.b64 x, {%2, %3};\n\t"
+      "mov.b64 m, {%4, %4};\n\t"
+      "mov.b64 d, {%5, %5};\n\t"
+      "fma.rn.f32x2 r, x, m, d;\n\t"
+      "mov.b64 {%0, %1}, r;\n\t}"
+      : "=f"(ra), "=f"(rb)
+      : "f"(a), "f"(b), "f"(s), "f"(c));
+}
+
 template <int XT>
 __device__ __forceinline__ uint4 dequant_word(uint32_t word, float s16, float nz) {
   uint32_t lo, hi;
   expand_nibbles(word, lo, hi);
-  const float w0 = fmaf(nibble_float<0>(lo), s16, nz), w1 = fmaf(nibble_float<0>(hi), s16, nz);
-  const float w2 = fmaf(nibble_float<1>(lo), s16, nz), w3 = fmaf(nibble_float<1>(hi), s16, nz);
-  const float w4 = fmaf(nibble_float<2>(lo), s16, nz), w5 = fmaf(nibble_float<2>(hi), s16, nz);
-  const float w6 = fmaf(nibble_float<3>(lo), s16, nz), w7 = fmaf(nibble_float<3>(hi), s16, nz);
+  float w0, w1, w2, w3, w4, w5, w6, w7;
+  fma2(nibble_float<0>(lo), nibble_float<0>(hi), s16, nz, w0, w1);
+  fma2(nibble_float<1>(lo), nibble_float<1>(hi), s16, nz, w2, w3);
+  fma2(nibble_float<2>(lo), nibble_float<2>(hi), s16, nz, w4, w5);
+  fma2(nibble_float<3>(lo), nibble_float<3>(hi), s16, nz, w6, w7);
   uint4 r;
   if constexpr (XT == QI4_DTYPE_F16) {
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r.x) : "f"(w1), "f"(w0));
