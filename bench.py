@@ -796,10 +796,12 @@ def profile_case(kind: str) -> None:
     device = torch.device("cuda", 0)
     lib = importlib.import_module(PACKAGE + "._lib").load()
     gen = torch.Generator(device=device).manual_seed(0)
-    if kind == "attention":
+    if kind in ("attention", "attention_b1"):
         # Config 4's decode attention: batch 64, 12 / 2 heads, 1024 past keys,
-        # two layers' caches (2 x 84 MB, more than L2) used alternately.
-        B, Hq, Hkv, D, cap, L = 64, 12, 2, 128, 1281, 1024
+        # two layers' caches (2 x 84 MB, more than L2) used alternately; or
+        # config 3's: batch 1, 640 past keys (the caches then fit L2 - the
+        # point there is the latency of a 20-CTA launch).
+        B, Hq, Hkv, D, cap, L = (64, 12, 2, 128, 1281, 1024) if kind == "attention" else (1, 12, 2, 128, 641, 640)
         bf = dict(dtype=torch.bfloat16, device=device)
         caches = [(torch.randn(B, Hkv, cap, D, generator=gen, device=device).to(torch.bfloat16),
                    torch.randn(B, Hkv, cap, D, generator=gen, device=device).to(torch.bfloat16)) for _ in range(2)]
@@ -880,11 +882,12 @@ def main() -> None:
     parser.add_argument("--no-configs", action="store_true",
                         help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, "
                              "AWQ down, batch-64 linears)")
-    parser.add_argument("--profile-case", choices=["gemv", "swiglu", "gemm", "attention", "lm_head"],
+    parser.add_argument("--profile-case", choices=["gemv", "swiglu", "gemm", "attention", "attention_b1", "lm_head"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
                              "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv; swiglu: gate/up pairs "
                              "fused) or M=2048 (gemm); "
-                             "4 decode-attention launches at batch 64 over 1024 keys (attention); 3 lm_head "
+                             "4 decode-attention launches at batch 64 over 1024 keys (attention; attention_b1: "
+                             "batch 1 over 640 keys); 3 lm_head "
                              "GEMV + argmax launches at batch 1 (lm_head)")
     args = parser.parse_args()
     if args.warmup < 3:
