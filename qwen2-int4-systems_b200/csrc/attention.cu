@@ -301,32 +301,59 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
 
 // A sequence whose cache is full (L_b >= cap) was not processed: its output
 // is zero (and qi4_device_status reports QI4_DEVICE_CACHE_FULL).
-__global__ void gqa_combine_kernel(const float* __restrict__ partial, const int32_t* __restrict__ lengths,
-                                   __nv_bfloat16* __restrict__ out, int Hkv, int G, int splits, int cap) {
+__global__ void __launch_bounds__(kD) gqa_combine_kernel(const float* __restrict__ partial,
+                                                          const int32_t* __restrict__ lengths,
+                                                          __nv_bfloat16* __restrict__ out, int Hkv, int G, int splits,
+                                                          int cap) {
   const int h = blockIdx.x, b = blockIdx.y;  // query head
   pdl_launch_dependents();
   pdl_wait();
   const int kvh = h / G, hg = h - kvh * G;
   const int L = lengths[b];
+  const int tid = threadIdx.x;  // output dim (blockDim = kD)
   if (L >= cap) {
-    for (int d = threadIdx.x; d < kD; d += blockDim.x) out[((int64_t)b * Hkv * G + h) * kD + d] = __float2bfloat16_rn(0.f);
-    if (threadIdx.x == 0 && h == 0) atomicOr(&g_attention_error, 2);
+    out[((int64_t)b * Hkv * G + h) * kD + tid] = __float2bfloat16_rn(0.f);
+    if (tid == 0 && h == 0) atomicOr(&g_attention_error, 2);
     return;
   }
   const int used = min(splits, (L + 1 + kSplitKeys - 1) / kSplitKeys);
-  const float* base = partial + ((int64_t)b * Hkv + kvh) * splits * G * (kD + 2) + hg * (kD + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < used; ++s) M = fmaxf(M, base[(int64_t)s * G * (kD + 2)]);
-  for (int d = threadIdx.x; d < kD; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < used; ++s) {
-      const float* p = base + (int64_t)s * G * (kD + 2);
-      const float f = p[0] == -INFINITY ? 0.f : __expf(p[0] - M);
-      num += p[2 + d] * f;
-      den += p[1] * f;
+  const int64_t stride = (int64_t)G * (kD + 2);  // between splits
+  const float* base = partial + ((int64_t)b * Hkv + kvh) * splits * stride + hg * (kD + 2);
+  // The largest running max over the splits (threads stride over splits; max is order-free).
+  __shared__ float red[kD / 32];
+  float mx = -INFINITY;
+  for (int sp = tid; sp < used; sp += kD) mx = fmaxf(mx, base[sp * stride]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int w = 1; w < kD / 32; ++w) M = fmaxf(M, red[w]);
+  // Per split (one thread each, a chunk of kD splits at a time): its weight
+  // e^(m - M) and sum l, in shared memory; then each thread sums its dim over
+  // the splits in split order (the loads of a chunk are independent).
+  __shared__ float f_s[kD], l_s[kD];
+  float num = 0.f, den = 0.f;
+  for (int c0 = 0; c0 < used; c0 += kD) {
+    const int n = min(kD, used - c0);
+    __syncthreads();  // the previous chunk's weights are consumed
+    if (tid < n) {
+      const float* p = base + (c0 + tid) * stride;
+      const float m = p[0];
+      f_s[tid] = m == -INFINITY ? 0.f : __expf(m - M);
+      l_s[tid] = p[1];
     }
-    out[((int64_t)b * Hkv * G + h) * kD + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    __syncthreads();
+    const float* pd = base + c0 * stride + 2 + tid;
+#pragma unroll 8
+    for (int sp = 0; sp < n; ++sp) {
+      const float f = f_s[sp];
+      num += pd[sp * stride] * f;
+      den += l_s[sp] * f;
+    }
   }
+  out[((int64_t)b * Hkv * G + h) * kD + tid] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
 }
 
 }  // namespace
