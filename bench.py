@@ -854,7 +854,7 @@ def profile_case(kind: str) -> None:
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": kind, "launches": 3, "m": 1}))
         return
-    m, algo = (1, 1) if kind == "gemv" else (2048, 2)
+    m, algo = {"gemv": (1, 1), "gemm": (2048, 2), "gemm_m64": (64, 2)}[kind]
     chain = Chain(lib, ents if kind == "gemv" else ents[:2], m, device, gen, algo=algo)
     for _ in range(3):
         chain.launch()
@@ -882,10 +882,10 @@ def main() -> None:
     parser.add_argument("--no-configs", action="store_true",
                         help="skip the secondary workload figures (gate M=1/4/16, seven shapes M=8..512, "
                              "AWQ down, batch-64 linears)")
-    parser.add_argument("--profile-case", choices=["gemv", "swiglu", "gemm", "attention", "attention_b1", "lm_head"],
+    parser.add_argument("--profile-case", choices=["gemv", "swiglu", "gemm", "gemm_m64", "attention", "attention_b1", "lm_head"],
                         help="run only a small case of one kernel for an ncu capture: 8 gate-shaped "
                              "weights (1536->8960, 59 MB), 3 chained launches at M=1 (gemv; swiglu: gate/up pairs "
-                             "fused) or M=2048 (gemm); "
+                             "fused), M=2048 (gemm) or M=64 (gemm_m64); "
                              "4 decode-attention launches at batch 64 over 1024 keys (attention; attention_b1: "
                              "batch 1 over 640 keys); 3 lm_head "
                              "GEMV + argmax launches at batch 1 (lm_head)")

@@ -13,22 +13,22 @@
 //   out[b, h] = softmax(q'_h . K[b, h / G]^T * scale + mask) V[b, h / G]
 //
 // over keys 0..L_b (the past and the new token), a key j counting only where
-// key_mask[b, j] is non-zero (left padding). FP32 scores, softmax and
-// accumulation; output bf16.
+// key_mask[b, j] is non-zero (left padding). FP32 scores (exact bf16
+// products), softmax and accumulation, the P.V products from 16-bit
+// softmax weights; output bf16.
 //
 // Work split ("flash decoding"): a CTA owns one (batch, KV head, 64-key
 // split) and all G query heads of that KV head, so K and V are read once for
 // the group (no expansion). The split's keys and values are copied into
 // shared memory (asynchronous 16-byte copies, all in flight while the queries
 // are rotated), rows padded so that the reads below are conflict-free.
-// Warps take 8 keys at a time (8 warps, one group each, for small grids,
-// whose duration is a warp's serial chain; 4 warps, two groups each,
-// otherwise): lane (key kk = lane % 8, quarter
-// dq = lane / 8) dots its 32 dims of the key with the G queries (held in
-// shared memory, FP32), a 2-step shuffle sums the quarters; per head an
-// online softmax (running max, rescaled sums) and P.V with lane = 4 output
-// dims. The CTA's partial (max, sum, 128 sums per head) goes to scratch; a
-// second kernel combines the splits per head. Both launch as programmatic
+// Four warps take 16 keys each on the tensor cores (mma.sync m16n8k16, bf16
+// operands, FP32 accumulators): scores Q K^T with the G query heads as the
+// rows of a zero-padded 16-row operand, an online softmax on the score
+// registers, and P.V with the FP32 weights split into two bf16 parts (high
+// and remainder: the products keep 16 bits of each weight). The CTA's
+// partial (max, sum, 128 sums per head) goes to scratch; a second kernel
+// combines the splits per head. Both launch as programmatic
 // dependents (the next kernel's prologue overlaps this one's tail).
 #include <algorithm>
 #include <cmath>
@@ -44,12 +44,8 @@ namespace {
 constexpr int kD = 128;          // head dim
 constexpr int kMaxGroup = 8;     // query heads per KV head
 constexpr int kSplitKeys = 64;   // keys per CTA
-// Warps per CTA: 8 (one 8-key group each per 64-key split) when the grid is
-// small - a batch-1 step runs ~20 CTAs, and a warp's serial chain of groups
-// is then the kernel's duration - else 4 (two groups each: less reduction
-// work and more CTAs resident per SM for large batches).
-constexpr int kWarpsSmallGrid = 8, kWarpsLargeGrid = 4;
-constexpr int kQPad = 36;        // floats per (head, quarter) row: 32 + 4 (bank spread)
+constexpr int kWarps = 4;        // per CTA: 16 keys of the split each
+constexpr int kQbStride = kD + 8;  // bf16 per staged query row (conflict-free fragment loads)
 
 struct AttnArgs {
   const __nv_bfloat16* q;      // [B, Hq, D]
@@ -84,12 +80,49 @@ __device__ __forceinline__ float rope(const __nv_bfloat16* x, const __nv_bfloat1
 
 constexpr int kRowBytes = kD * 2 + 16;  // a staged key / value row, padded (conflict-free 16-byte reads)
 
+// D += A B, m16n8k16, bf16 operands, FP32 accumulators (A rows = query
+// heads padded to 16, B = keys or values).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four 8x8 bf16 matrices from shared memory, transposed (lane l gives the
+// row address of matrix l / 8, row l % 8).
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// The 8x8 b16 matrix held in fragment layout (lane = row * 4 + column pair),
+// transposed.
+__device__ __forceinline__ uint32_t movm_trans(uint32_t x) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int kWarps>
-__global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs a) {
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__global__ void __launch_bounds__(kWarps * 32, 5) gqa_decode_kernel(const AttnArgs a) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   // Programmatic dependent launch: the next kernel may start its prologue;
   // this one waits for its predecessor (the q/k/v projections) before it
@@ -107,12 +140,14 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   __shared__ __align__(16) uint8_t kv_s[2][kSplitKeys][kRowBytes];  // past keys / values of the split
-  __shared__ __align__(16) float q_s[kMaxGroup][4][kQPad];          // RoPE'd queries, FP32, by head and quarter
-  __shared__ float p_s[kWarps][8][kMaxGroup];                       // softmax weights of a warp's 8 keys
-  __shared__ float red_m[kWarps][kMaxGroup], red_l[kWarps][kMaxGroup];
-  // After the key loop the staged rows are dead: the warps' partial sums reuse them.
-  static_assert(sizeof(float) * kWarps * kMaxGroup * kD <= sizeof(uint8_t) * 2 * kSplitKeys * kRowBytes, "");
-  auto red_acc = reinterpret_cast<float (*)[kMaxGroup][kD]>(&kv_s[0][0][0]);
+  __shared__ __align__(16) __nv_bfloat16 qb[kMaxGroup][kQbStride];  // RoPE'd queries (rows G.. zero)
+  __shared__ float red_m[kWarps][kMaxGroup], red_l[kWarps][kMaxGroup], red_f[kWarps][kMaxGroup];
+  // After the key loop the staged rows are dead: the warps' partial sums
+  // reuse them (rows padded by 4 floats: a warp's stores to its heads' rows
+  // fall in different banks).
+  constexpr int kAccStride = kD + 4;
+  static_assert(sizeof(float) * kWarps * kMaxGroup * kAccStride <= sizeof(uint8_t) * 2 * kSplitKeys * kRowBytes, "");
+  auto red_acc = reinterpret_cast<float (*)[kMaxGroup][kAccStride]>(&kv_s[0][0][0]);
 
   // 1. The split's past keys and values: all copies in flight at once.
   const __nv_bfloat16* kbase = a.k_cache + b * a.cb + kvh * a.ch;
@@ -153,7 +188,17 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
   // appended to the cache), from shared memory.
   for (int i = tid; i < G * kD; i += blockDim.x) {
     const int h = i / kD, d = i - h * kD;
-    q_s[h][d >> 5][d & 31] = rope_on ? rope(qraw_s[h], cs_s, sn_s, d) : bf(qraw_s[h][d]);
+    const float v = rope_on ? rope(qraw_s[h], cs_s, sn_s, d) : bf(qraw_s[h][d]);  // a bf16 value either way
+    qb[h][d] = __float2bfloat16_rn(v);
+  }
+  {
+    // Rows G..7 of the query operand are zero; value rows past the split's
+    // last key, up to the warp's 16-key boundary, are zero (their weights are
+    // zero, and 0 x a stale NaN pattern would not be).
+    for (int i = tid; i < (kMaxGroup - G) * kD; i += blockDim.x) qb[G + i / kD][i % kD] = __float2bfloat16_rn(0.f);
+    const int nv = k1 - k0, nz = ((nv + 15) & ~15) - nv;
+    for (int i = tid; i < nz * 16; i += blockDim.x)
+      *reinterpret_cast<uint4*>(&kv_s[1][nv + (i >> 4)][(i & 15) * 16]) = make_uint4(0u, 0u, 0u, 0u);
   }
   if (has_new) {
     __nv_bfloat16* kc = a.k_cache + b * a.cb + kvh * a.ch + (int64_t)L * kD;
@@ -170,132 +215,132 @@ __global__ void __launch_bounds__(kWarps * 32) gqa_decode_kernel(const AttnArgs 
   }
   __syncthreads();
 
-  // 3. Keys 8 at a time per warp: lane (key kk = lane % 8, quarter dq = lane / 8).
-  const int kk = lane & 7, dq = lane >> 3;
-  float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][4];
+  // 3. Tensor cores: a warp takes 16 keys at a time (m16n8k16, bf16
+  // operands, FP32 accumulators), with the keys / dims as the 16 rows and the
+  // query heads as the 8 columns (heads G..7 zero). Scores S^T = K Q^T: lane
+  // (gq = lane / 4, tq = lane % 4) holds keys gq and gq + 8 for heads 2tq,
+  // 2tq + 1. Online softmax per head over the 16 keys (shuffles across gq).
+  // O^T = V^T P^T: V^T fragments are transposed loads of the staged rows; the
+  // weights, split into bf16 high and remainder parts (16 bits of each
+  // weight reach the products), move into operand layout with in-register
+  // 8x8 transposes.
+  const int gq = lane >> 2, tq = lane & 3;
+  uint32_t qf[kD / 16][2];  // Q^T operand per 16-dim step
 #pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[h][j] = 0.f;
+  for (int ks = 0; ks < kD / 16; ++ks) {
+    qf[ks][0] = *reinterpret_cast<const uint32_t*>(&qb[gq][ks * 16 + 2 * tq]);
+    qf[ks][1] = *reinterpret_cast<const uint32_t*>(&qb[gq][ks * 16 + 2 * tq + 8]);
   }
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, o[kD / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < kD / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
   const uint8_t* mrow = a.key_mask ? a.key_mask + (int64_t)b * a.mask_stride : nullptr;
-  for (int g0 = k0 + warp * 8; g0 < k1; g0 += kWarps * 8) {
-    const int key = g0 + kk;
-    const bool valid = key < k1 && (!mrow || mrow[key] != 0);
-    float s[kMaxGroup];
+  // ldmatrix lane addresses: matrix j = lane / 8 covers rows + (j % 2) * 8, columns + (j / 2) * 8.
+  const int lrow = (lane & 7) + (((lane >> 3) & 1) << 3), lcol = (lane >> 4) << 4;  // column in bytes
+  const uint32_t ks_base = smem_addr_u(&kv_s[0][0][0]) + lrow * kRowBytes + lcol;
+  const uint32_t vs_base = smem_addr_u(&kv_s[1][0][0]) + lrow * kRowBytes + lcol;
+  for (int g0 = k0 + warp * 16; g0 < k1; g0 += kWarps * 16) {
+    const int r0 = g0 - k0;
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) s[h] = 0.f;
-    if (key < k1) {
-      float kf[32];
-      const uint4* kp = reinterpret_cast<const uint4*>(&kv_s[0][key - k0][dq * 64]);
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3;  // K rows r0.. (keys), dims 16 ks..: matrices (keys +0, +8) x (dims +0, +8)
+      ldsm_x4(ks_base + r0 * kRowBytes + ks * 32, a0, a1, a2, a3);
+      mma_bf16(sc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+    }
+    float mx[2];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 w = kp[c];
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    for (int r = 0; r < 2; ++r) {  // key g0 + gq + 8 r
+      const int key = g0 + gq + 8 * r;
+      const bool valid = key < k1 && (!mrow || mrow[key] != 0);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          kf[c * 8 + 2 * e] = __uint_as_float(ws[e] << 16);
-          kf[c * 8 + 2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) {
-        if (h < G) {
-          const float4* qh = reinterpret_cast<const float4*>(&q_s[h][dq][0]);
-          float t = 0.f;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float4 qv = qh[c];
-            t = fmaf(qv.x, kf[4 * c], t);
-            t = fmaf(qv.y, kf[4 * c + 1], t);
-            t = fmaf(qv.z, kf[4 * c + 2], t);
-            t = fmaf(qv.w, kf[4 * c + 3], t);
-          }
-          s[h] = t;
-        }
-      }
+      for (int e = 0; e < 2; ++e) sc[2 * r + e] = valid ? sc[2 * r + e] * a.scale : -INFINITY;
     }
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 8);
-      s[h] += __shfl_xor_sync(0xffffffffu, s[h], 16);
-      s[h] = valid ? s[h] * a.scale : -INFINITY;
+    for (int e = 0; e < 2; ++e) {  // head 2tq + e
+      float t = fmaxf(sc[e], sc[2 + e]);
+      t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 4));
+      t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 8));
+      mx[e] = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, 16));
     }
-    // Online softmax over this group of 8 keys, per head.
+    float alpha[2], p[4];
 #pragma unroll
-    for (int h = 0; h < kMaxGroup; ++h) {
-      if (h >= G) continue;
-      float mx = s[h];
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-      const float mn = fmaxf(m[h], mx);
-      const float alpha = mn == -INFINITY ? 1.f : __expf(m[h] - mn);
-      const float p = s[h] == -INFINITY ? 0.f : __expf(s[h] - mn);
-      m[h] = mn;
-      l[h] = l[h] * alpha + p;  // per key kk (replicated over dq); summed over kk at the end
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[h][j] *= alpha;
-      if (dq == 0) p_s[warp][kk][h] = p;
+    for (int e = 0; e < 2; ++e) {
+      const float mn = fmaxf(m[e], mx[e]);
+      alpha[e] = mn == -INFINITY ? 1.f : __expf(m[e] - mn);
+      m[e] = mn;
+      p[e] = sc[e] == -INFINITY ? 0.f : __expf(sc[e] - mn);
+      p[2 + e] = sc[2 + e] == -INFINITY ? 0.f : __expf(sc[2 + e] - mn);
+      l[e] = l[e] * alpha[e] + (p[e] + p[2 + e]);  // this lane's two keys; summed over gq at the end
     }
-    __syncwarp();
-    // P.V: lane owns output dims 4 lane .. 4 lane + 3.
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int key2 = g0 + e;
-      if (key2 >= k1) break;
-      const uint2 w = *reinterpret_cast<const uint2*>(&kv_s[1][key2 - k0][lane * 8]);
-      const float vf[4] = {__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u),
-                           __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xFFFF0000u)};
-#pragma unroll
-      for (int h = 0; h < kMaxGroup; ++h) {
-        if (h >= G) continue;
-        const float p = p_s[warp][e][h];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[h][j] = fmaf(p, vf[j], acc[h][j]);
-      }
+    for (int mt = 0; mt < kD / 16; ++mt) {
+      o[mt][0] *= alpha[0];
+      o[mt][1] *= alpha[1];
+      o[mt][2] *= alpha[0];
+      o[mt][3] *= alpha[1];
     }
-    __syncwarp();
+    // P^T operand: rows = keys 2tq.., column = head gq; high and remainder parts.
+    const uint32_t h0 = bf16x2(p[0], p[1]), h1 = bf16x2(p[2], p[3]);
+    const uint32_t r0w = bf16x2(p[0] - __uint_as_float(h0 << 16), p[1] - __uint_as_float(h0 & 0xFFFF0000u));
+    const uint32_t r1w = bf16x2(p[2] - __uint_as_float(h1 << 16), p[3] - __uint_as_float(h1 & 0xFFFF0000u));
+    const uint32_t bh0 = movm_trans(h0), bh1 = movm_trans(h1), bl0 = movm_trans(r0w), bl1 = movm_trans(r1w);
+#pragma unroll
+    for (int mt = 0; mt < kD / 16; ++mt) {
+      uint32_t a0, a1, a2, a3;  // V^T: transposed loads of rows (keys +0, +8) x (dims +0, +8)
+      ldsm_x4_trans(vs_base + r0 * kRowBytes + mt * 32, a0, a2, a1, a3);
+      mma_bf16(o[mt], a0, a1, a2, a3, bh0, bh1);
+      mma_bf16(o[mt], a0, a1, a2, a3, bl0, bl1);
+    }
   }
   __syncthreads();  // every warp is done with the staged rows
-  // Per warp: sum l over the 8 key lanes (each value is replicated 4 times).
 #pragma unroll
-  for (int h = 0; h < kMaxGroup; ++h) {
-    if (h >= G) continue;
-    float t = l[h];
-    t += __shfl_xor_sync(0xffffffffu, t, 1);
-    t += __shfl_xor_sync(0xffffffffu, t, 2);
-    t += __shfl_xor_sync(0xffffffffu, t, 4);
-    if (lane == 0) {
-      red_m[warp][h] = m[h];
-      red_l[warp][h] = t;
+  for (int e = 0; e < 2; ++e) {
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 4);
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 8);
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 16);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int h = 2 * tq + e;
+    if (h < G) {
+      if (gq == 0) {
+        red_m[warp][h] = m[e];
+        red_l[warp][h] = l[e];
+      }
+#pragma unroll
+      for (int mt = 0; mt < kD / 16; ++mt) {
+        red_acc[warp][h][mt * 16 + gq] = o[mt][e];
+        red_acc[warp][h][mt * 16 + gq + 8] = o[mt][2 + e];
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) red_acc[warp][h][lane * 4 + j] = acc[h][j];
   }
   __syncthreads();
-  // Combine the warps into the CTA's partial (warps without keys have m = -inf).
+  // Combine the warps into the CTA's partial (warps without keys have m = -inf):
+  // per head the running max, each warp's weight e^(m_w - max) and the sum.
   float* out = a.partial + (((int64_t)b * a.Hkv + kvh) * a.splits + split) * G * (kD + 2);
-  for (int i = tid; i < G * kD; i += blockDim.x) {
-    const int h = i / kD, d = i - h * kD;
+  if (tid < G) {
+    const int h = tid;
     float mm = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, red_m[w][h]);
-    float ls = 0.f, as = 0.f;
+    float ls = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       const float f = red_m[w][h] == -INFINITY ? 0.f : __expf(red_m[w][h] - mm);
+      red_f[w][h] = f;
       ls += red_l[w][h] * f;
-      as += red_acc[w][h][d] * f;
     }
-    float* o = out + h * (kD + 2);
-    o[2 + d] = as;
-    if (d == 0) {
-      o[0] = mm;
-      o[1] = ls;
-    }
+    out[h * (kD + 2)] = mm;
+    out[h * (kD + 2) + 1] = ls;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * kD; i += blockDim.x) {
+    const int h = i / kD, d = i - h * kD;
+    float as = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) as += red_acc[w][h][d] * red_f[w][h];
+    out[h * (kD + 2) + 2 + d] = as;
   }
 }
 
@@ -393,16 +438,11 @@ cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_ne
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, Hkv, B);
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const bool small = (int64_t)a.splits * Hkv * B <= 2 * (int64_t)sms;
-  cfg.blockDim = dim3((small ? kWarpsSmallGrid : kWarpsLargeGrid) * 32, 1, 1);
+  cfg.blockDim = dim3(kWarps * 32, 1, 1);
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = small ? cudaLaunchKernelEx(&cfg, gqa_decode_kernel<kWarpsSmallGrid>, a)
-                        : cudaLaunchKernelEx(&cfg, gqa_decode_kernel<kWarpsLargeGrid>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_decode_kernel, a);
   if (e != cudaSuccess) return e;
   cfg.gridDim = dim3(Hq, B, 1);
   cfg.blockDim = dim3(kD, 1, 1);

@@ -66,6 +66,7 @@ __host__ __device__ constexpr int p_stages(int x_tiles, int bn) {
   return x_tiles * bn <= 64 ? 5 : x_tiles * bn <= 128 ? 3 : x_tiles * bn <= 192 ? 4 : 2;
 }
 constexpr int kTileN = 128;     // weight rows per tile (UMMA M)
+constexpr int kMaxKSplit = 8;   // CTAs per cluster along K (portable cluster size)
 // Dequantise/epilogue warps per CTA: 16 (one CTA per SM, tiles up to 256
 // tokens) or 8 (128-token tiles, two CTAs per SM, so that one CTA's prologue
 // and epilogue overlap the other's main loop). Threads: producer + MMA warps
@@ -272,7 +273,9 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
   uint64_t* acc_full = p_empty + kPStages;  // final commit -> epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
-  float* part = reinterpret_cast<float*>(tmem_slot + 4);  // [BN][128] FP32 partial tile (K split only)
+  // [BN][128] FP32 partial tile (K split only), 16-byte aligned for the cluster's vector reads.
+  uint8_t* part_raw = reinterpret_cast<uint8_t*>(tmem_slot + 4);
+  float* part = reinterpret_cast<float*>(part_raw + ((16u - (smem_addr(part_raw) & 15u)) & 15u));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // This CTA's matrix and its 128-row tile within that matrix.
@@ -497,24 +500,47 @@ __global__ void __launch_bounds__(gemm_threads(DW), DW == 8 ? 2 : 1)
 
   if (a.ksplit > 1) {
     // K split: the cluster's CTAs sum their partial tiles over distributed
-    // shared memory; CTA z finishes rows [z * 128 / ksplit, ...) of the tile.
+    // shared memory; CTA z finishes rows [z * per, (z + 1) * per) of the tile
+    // (per a multiple of 4). A thread takes 4 consecutive rows of one token:
+    // it issues the 16-byte loads from every CTA of the cluster before
+    // summing them in rank order.
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();  // every partial tile is written
     if (warp >= 2) {
       const int nranks = (int)cluster.num_blocks();
-      const int per = (kTileN + nranks - 1) / nranks;
+      const int per = ((kTileN + nranks - 1) / nranks + 3) & ~3;
       const int rlo = (int)cluster.block_rank() * per;
-      const int rows = min(kTileN, rlo + per) - rlo;
-      for (int i = (int)threadIdx.x - 64; rows > 0 && i < rows * BN; i += 32 * DW) {
-        const int c = i / rows, r = rlo + (i - c * rows);
-        float sum = 0.f;
-        for (int q = 0; q < nranks; ++q) sum += cluster.map_shared_rank(part, q)[c * kTileN + r];
+      const int rows4 = max(0, min(kTileN, rlo + per) - rlo) / 4;
+      const float4* peer[kMaxKSplit];
+#pragma unroll
+      for (int q = 0; q < kMaxKSplit; ++q)
+        peer[q] = reinterpret_cast<const float4*>(cluster.map_shared_rank(part, q < nranks ? q : 0));
+      for (int i = (int)threadIdx.x - 64; i < rows4 * BN; i += 32 * DW) {
+        const int c = i / rows4, r = rlo + 4 * (i - c * rows4);
+        float4 v[kMaxKSplit];
+#pragma unroll
+        for (int q = 0; q < kMaxKSplit; ++q)
+          if (q < nranks) v[q] = peer[q][(c * kTileN + r) >> 2];
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < kMaxKSplit; ++q)
+          if (q < nranks) {
+            sum[0] += v[q].x;
+            sum[1] += v[q].y;
+            sum[2] += v[q].z;
+            sum[3] += v[q].w;
+          }
         const int m = m0 + c;
-        const int64_t n = n0 + r;
-        if (m < a.M && n < N) {
-          const float b = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, n) : 0.f;
-          store_from_f32(mt.out, a.out_dtype, (int64_t)m * N + n, sum + b);
+        if (m < a.M) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int64_t n = n0 + r + e;
+            if (n < N) {
+              const float b = mt.bias ? load_as_f32(mt.bias, a.bias_dtype, n) : 0.f;
+              store_from_f32(mt.out, a.out_dtype, (int64_t)m * N + n, sum[e] + b);
+            }
+          }
         }
       }
     }
@@ -534,7 +560,7 @@ size_t smem_bytes(int BN, int x_tiles, int ksplit) {
   const int ps = p_stages(x_tiles, BN), st = a_stages(x_tiles, BN);
   return 1024 + (size_t)st * x_tiles * BN * 128 + (size_t)ps * kPBytes +
          (3 * st + 2 * ps + 1) * sizeof(uint64_t) + 16 +
-         (ksplit > 1 ? (size_t)BN * kTileN * sizeof(float) : 0);
+         (ksplit > 1 ? (size_t)BN * kTileN * sizeof(float) + 16 : 0);
 }
 
 template <int XT, int BN, int DW>

@@ -120,3 +120,28 @@ def test_tc_fp32_activations_down_proj_path(b200, cuda_device, m, n, k):
     got = _run(b200, cuda_device, x, qw, sc, z, None, n, k)
     assert got.dtype == torch.float32
     assert_linear_close(got, _ref(x, qw, sc, z, None, n, k), 2e-2, f"tc fp32 {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize(("bn", "ks"), [(32, 2), (64, 2), (64, 3), (64, 5), (64, 8), (128, 4), (128, 7)])
+def test_tc_k_split_clusters(b200, cuda_device, bn, ks, dtype):
+    """Every tile width and cluster size of the K split (forced through the
+    plan override): the cluster's partial tiles summed over distributed
+    shared memory, rows shared out in multiples of 4, bias added once; a
+    ragged N and a K whose boxes do not divide evenly over the cluster."""
+    from importlib import import_module
+
+    lib = import_module(b200.__name__ + "._lib").load()
+    m, n, k = 70, 1000, 8960 - 64 * 5
+    qw, sc, z = _weights(k, n, "asym", 71)
+    g = torch.Generator().manual_seed(bn * 10 + ks)
+    x = torch.randn(m, k, generator=g).to(dtype)
+    bias = (torch.randn(n, generator=g) * 0.05).to(torch.bfloat16) if dtype == torch.bfloat16 else None
+    assert lib.qi4_gemm_tc_plan_override(bn, ks) == 0
+    try:
+        got = _run(b200, cuda_device, x, qw, sc, z, bias, n, k)
+        torch.cuda.synchronize()
+    finally:
+        lib.qi4_gemm_tc_plan_override(0, 0)
+    assert lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+    assert_linear_close(got, _ref(x, qw, sc, z, bias, n, k), 2e-2, f"tc k-split bn={bn} ks={ks} {dtype}")
