@@ -317,6 +317,15 @@ QI4_API int qi4_bf16_gemv_argmax(const void* weight, const void* x, int64_t M, i
 QI4_API int qi4_bf16_gemv_argmax_ws(const void* weight, const void* x, int64_t M, int64_t K, int64_t N, void* logits,
                                     int64_t* argmax, uint64_t* keys, void* stream);
 
+/* Greedy pick over bf16 logits rows, for batches the lm_head GEMV does not
+ * take (the tied lm_head is then a library bf16 GEMM into `logits`): out[b] =
+ * torch.argmax(logits[b, :V]) - the first index of the largest value, a NaN
+ * counting as larger than every number. Rows are `ld` elements apart (ld >=
+ * V). One CTA per row, programmatic dependent launch. Replaces the greedy
+ * pick of reference src/qwen_int4/generation.py:51 (logits[:, -1].argmax).
+ * Returns QI4_ERR_SHAPE unless 1 <= B < 2^31, 1 <= V < 2^32, ld >= V. */
+QI4_API int qi4_bf16_argmax_rows(const void* logits, int64_t B, int64_t V, int64_t ld, int64_t* out, void* stream);
+
 /* Tuning hook: forces the TMA/tensor-pipe GEMV launch shape for subsequent
  * calls made by the calling thread - output rows per CTA (16, 32, 64 or 128),
  * K-split factor (CTAs per cluster, 1..8) and warps per CTA (2, 4, 8, 16 or

@@ -45,6 +45,7 @@ SIGNATURES = {
                                     _i64, _i64, ctypes.c_float, _i, _p, _sz, _p],
     "qi4_bf16_gemv_argmax": [_p, _p, _i64, _i64, _i64, _p, _p, _p],
     "qi4_bf16_gemv_argmax_ws": [_p, _p, _i64, _i64, _i64, _p, _p, _p, _p],
+    "qi4_bf16_argmax_rows": [_p, _i64, _i64, _i64, _p, _p],
     "qi4_add_rmsnorm": [_p, _p, _i, _p, _p, _i64, _i64, ctypes.c_float, _p],
     "qi4_w4g64_linear_multi_norm": [_p, _i64, _i64, _i, _p, _p, _p, _p, _i, _p, _p, _p],
     "qi4_w4g64_gate_up_silu_norm": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],

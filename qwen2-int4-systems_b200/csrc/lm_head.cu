@@ -153,6 +153,65 @@ __global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t* out, i
   }
 }
 
+// Row-wise argmax of bf16 logits (torch.argmax(dim=-1): the first index of
+// the largest value, a NaN counting as larger than every number). One CTA
+// per row; a thread keeps the best 64-bit key of its elements (order-
+// preserving value bits over the inverted index: the largest key is the
+// largest value at the smallest index), then warp shuffles and a pass over
+// the warps' keys. 16-byte loads when the rows allow them.
+constexpr int kArgmaxThreads = 1024;
+
+__device__ __forceinline__ unsigned long long argmax_key(uint32_t bits16, int64_t i) {
+  const float v = __uint_as_float(bits16 << 16);
+  const uint32_t o = v != v ? 0xFFFFFFFFu : ordered(v);
+  return ((unsigned long long)o << 32) | (0xFFFFFFFFull - (unsigned long long)i);
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const uint16_t* __restrict__ logits, int64_t V,
+                                                                     int64_t ld, int64_t* __restrict__ out,
+                                                                     int vec) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint16_t* row = logits + (int64_t)blockIdx.x * ld;
+  unsigned long long best = 0;
+  if (vec) {
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    for (int64_t c = threadIdx.x; c < V / 8; c += kArgmaxThreads) {
+      const uint4 w = __ldg(r4 + c);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const unsigned long long k0 = argmax_key(ws[e] & 0xFFFFu, c * 8 + 2 * e);
+        const unsigned long long k1 = argmax_key(ws[e] >> 16, c * 8 + 2 * e + 1);
+        best = k0 > best ? k0 : best;
+        best = k1 > best ? k1 : best;
+      }
+    }
+    for (int64_t i = V / 8 * 8 + threadIdx.x; i < V; i += kArgmaxThreads) {
+      const unsigned long long k = argmax_key(row[i], i);
+      best = k > best ? k : best;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += kArgmaxThreads) {
+      const unsigned long long k = argmax_key(row[i], i);
+      best = k > best ? k : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long wk[kArgmaxThreads / 32];
+  if ((threadIdx.x & 31) == 0) wk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = wk[0];
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) b = wk[w] > b ? wk[w] : b;
+    out[blockIdx.x] = (int64_t)(0xFFFFFFFFull - (b & 0xFFFFFFFFull));
+  }
+}
+
 cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, cudaLaunchAttribute* attr) {
   attr->id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr->val.programmaticStreamSerializationAllowed = 1;
@@ -263,4 +322,31 @@ extern "C" QI4_API int qi4_bf16_gemv_argmax_ws(const void* weight, const void* x
     return QI4_ERR_ARGUMENT;
   }
   return lm_head_impl(weight, x, M, K, N, logits, argmax, reinterpret_cast<unsigned long long*>(keys), stream_ptr);
+}
+
+extern "C" QI4_API int qi4_bf16_argmax_rows(const void* logits, int64_t B, int64_t V, int64_t ld, int64_t* out,
+                                            void* stream_ptr) {
+  using namespace qi4;
+  clear_error();
+  if (!logits || !out) {
+    set_error("logits and out must be non-null");
+    return QI4_ERR_ARGUMENT;
+  }
+  if (B < 1 || B > INT32_MAX || V < 1 || V >= (int64_t)1 << 32 || ld < V) {
+    set_error("argmax_rows takes 1 <= B < 2^31, 1 <= V < 2^32 and a row pitch ld >= V (got B=%lld V=%lld ld=%lld)",
+              (long long)B, (long long)V, (long long)ld);
+    return QI4_ERR_SHAPE;
+  }
+  const int vec = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && ld % 8 == 0;
+  cudaLaunchAttribute attr;
+  const cudaLaunchConfig_t cfg =
+      pdl_config(dim3((unsigned)B), dim3(kArgmaxThreads), 0, static_cast<cudaStream_t>(stream_ptr), &attr);
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, argmax_rows_kernel, static_cast<const uint16_t*>(logits), V, ld, out, vec);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("argmax_rows launch failed: %s", cudaGetErrorString(e));
+    return QI4_ERR_LAUNCH;
+  }
+  return QI4_OK;
 }

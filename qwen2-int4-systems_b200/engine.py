@@ -18,7 +18,7 @@ library's kernels, on static buffers:
            (qi4_w4g64_linear on FP32 input)
         -> final residual add + RMSNorm -> tied lm_head + greedy argmax
            (qi4_bf16_gemv_argmax for up to 8 sequences; a bf16 matmul and
-           argmax beyond) -> next tokens, lengths and positions advanced on
+           qi4_bf16_argmax_rows beyond) -> next tokens, lengths and positions advanced on
            the device.
 
 The prompt runs through the reference model itself (``model(..., use_cache=
@@ -100,6 +100,10 @@ class DecodeEngine:
         self.hm = torch.empty(B, inter, dtype=torch.float32, device=dev)
         self.y = torch.empty(B, self.D, dtype=torch.float32, device=dev)
         self.next = torch.zeros(B, dtype=torch.int64, device=dev)
+        # Beyond the GEMV's 8 tokens the tied lm_head is a bf16 matmul into
+        # these logits, then qi4_bf16_argmax_rows.
+        self.logits = (torch.empty(B, self.lm_weight.shape[0], dtype=torch.bfloat16, device=dev)
+                       if B > 8 else None)
         self.lengths = torch.zeros(B, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(B, dtype=torch.int32, device=dev)
         self.key_mask = torch.zeros(B, max_len, dtype=torch.uint8, device=dev)
@@ -189,7 +193,10 @@ class DecodeEngine:
                                            self.lm_keys.data_ptr(), self._s)
             _lib.check(rc, "qi4_bf16_gemv_argmax")
         else:
-            torch.argmax(torch.nn.functional.linear(self.x, self.lm_weight), dim=-1, out=self.next)
+            torch.mm(self.x, self.lm_weight.t(), out=self.logits)
+            rc = L.qi4_bf16_argmax_rows(self.logits.data_ptr(), B, self.logits.shape[1], self.logits.shape[1],
+                                        self.next.data_ptr(), self._s)
+            _lib.check(rc, "qi4_bf16_argmax_rows")
         self.lengths.add_(1)
         self.positions.add_(1)
         self.tokens.copy_(self.next)

@@ -64,3 +64,38 @@ def test_argmax_with_caller_workspace_leaves_it_zero(b200, cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(a, b) and int(keys.abs().sum()) == 0
     assert lib.qi4_bf16_gemv_argmax_ws(w.data_ptr(), x.data_ptr(), 1, 1536, 151936, None, b.data_ptr(), None, s) == -1
+
+
+@pytest.mark.parametrize(("b", "v", "pad", "offset"), [(64, 151936, 0, 0), (3, 1001, 7, 1), (1, 7, 0, 0), (9, 64, 8, 0)])
+def test_argmax_rows_matches_torch_argmax(b200, cuda_device, b, v, pad, offset):
+    """qi4_bf16_argmax_rows against torch.argmax(dim=-1) on bf16 rows: planted
+    ties (the first index wins), NaN (counts as the maximum), +/-inf, rows
+    with a pitch above V and a base that is not 16-byte aligned (the scalar
+    path)."""
+    from importlib import import_module
+
+    lib = import_module(b200.__name__ + "._lib").load()
+    g = torch.Generator().manual_seed(b * 7 + v)
+    ld = v + pad
+    buf = (torch.randn(b * ld + offset, generator=g) * 4).to(torch.bfloat16).to(cuda_device)
+    rows = buf[offset:].view(b, ld)
+    top = rows[:, :v].float().max(dim=-1).values
+    for r in range(b):
+        if r % 4 == 1 and v > 3:  # a tie with the existing maximum, later and earlier
+            i = int(rows[r, :v].float().argmax())
+            rows[r, (i + 1) % v] = top[r].to(torch.bfloat16)
+            rows[r, max(i - 1, 0)] = top[r].to(torch.bfloat16)
+        if r % 4 == 2:
+            rows[r, v // 2] = float("nan")
+            rows[r, v - 1] = float("nan")
+        if r % 4 == 3:
+            rows[r, 0] = float("-inf")
+            rows[r, v - 1] = float("inf")
+    if pad:
+        rows[:, v:] = 1e4  # past V: never read
+    out = torch.full((b,), -5, dtype=torch.int64, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.qi4_bf16_argmax_rows(rows.data_ptr(), b, v, ld, out.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.argmax(rows[:, :v], dim=-1))
+    assert lib.qi4_bf16_argmax_rows(rows.data_ptr(), b, v, v - 1, out.data_ptr(), s) != 0  # ld < V
