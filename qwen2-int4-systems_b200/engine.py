@@ -202,6 +202,10 @@ class DecodeEngine:
         self.tokens.copy_(self.next)
 
     def _capture(self):
+        # The capture stream first waits for the caller's stream: the prefill's
+        # cache copies, lengths, positions and tokens must have landed before
+        # the warm-up step reads them and before they are saved for restoring.
+        self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             # Warm-up outside capture, on a state that is restored afterwards.
             saved = (self.lengths.clone(), self.positions.clone(), self.key_mask.clone(), self.tokens.clone())

@@ -60,3 +60,25 @@ def test_engine_full_qwen2_batch1(b200, cuda_device):
     engine = eng_mod.DecodeEngine(model, batch=1, max_len=64)
     seq = engine.generate(prompt, 16)
     _check_teacher_forced(model, seq, 32)
+
+
+def test_engine_instances_in_sequence_after_prefill(b200, cuda_device):
+    """Engines built one after another in a process, each capturing its step
+    graph right after a long prefill (the full Qwen2-1.5B, 16 x 256 tokens):
+    every one agrees with the reference model teacher-forced and with the
+    others. The capture stream must wait for the prefill's writes before its
+    warm-up step reads and saves the decode state."""
+    q2 = importlib.import_module(b200.__name__ + ".qwen2")
+    eng_mod = importlib.import_module(b200.__name__ + ".engine")
+    model = q2.build_random_qwen2(device=cuda_device, seed=0)
+    prompt = torch.randint(0, model.config.vocab_size, (16, 256),
+                           generator=torch.Generator().manual_seed(1)).to(cuda_device)
+    seqs = []
+    for _ in range(3):
+        engine = eng_mod.DecodeEngine(model, batch=16, max_len=280)
+        seqs.append(engine.generate(prompt, 8))
+        engine.close()
+        del engine
+    for seq in seqs:
+        _check_teacher_forced(model, seq, 256)
+    assert torch.equal(seqs[0], seqs[1]) and torch.equal(seqs[1], seqs[2])
