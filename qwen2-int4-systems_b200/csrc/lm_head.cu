@@ -159,7 +159,7 @@ __global__ void argmax_finalize_kernel(unsigned long long* keys, int64_t* out, i
 // preserving value bits over the inverted index: the largest key is the
 // largest value at the smallest index), then warp shuffles and a pass over
 // the warps' keys. 16-byte loads when the rows allow them.
-constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxThreads = 1024, kArgmaxLoads = 8;
 
 __device__ __forceinline__ unsigned long long argmax_key(uint32_t bits16, int64_t i) {
   const float v = __uint_as_float(bits16 << 16);
@@ -175,16 +175,29 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const uint1
   const uint16_t* row = logits + (int64_t)blockIdx.x * ld;
   unsigned long long best = 0;
   if (vec) {
+    // kArgmaxLoads 16-byte loads of a thread in flight at once (a row is one
+    // CTA's: its bytes in flight set the row's speed).
     const uint4* r4 = reinterpret_cast<const uint4*>(row);
-    for (int64_t c = threadIdx.x; c < V / 8; c += kArgmaxThreads) {
-      const uint4 w = __ldg(r4 + c);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    const int64_t n16 = V / 8;
+    for (int64_t c0 = threadIdx.x; c0 < n16; c0 += (int64_t)kArgmaxThreads * kArgmaxLoads) {
+      uint4 w[kArgmaxLoads];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const unsigned long long k0 = argmax_key(ws[e] & 0xFFFFu, c * 8 + 2 * e);
-        const unsigned long long k1 = argmax_key(ws[e] >> 16, c * 8 + 2 * e + 1);
-        best = k0 > best ? k0 : best;
-        best = k1 > best ? k1 : best;
+      for (int u = 0; u < kArgmaxLoads; ++u) {
+        const int64_t c = c0 + (int64_t)u * kArgmaxThreads;
+        w[u] = c < n16 ? __ldg(r4 + c) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kArgmaxLoads; ++u) {
+        const int64_t c = c0 + (int64_t)u * kArgmaxThreads;
+        if (c >= n16) break;
+        const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const unsigned long long k0 = argmax_key(ws[e] & 0xFFFFu, c * 8 + 2 * e);
+          const unsigned long long k1 = argmax_key(ws[e] >> 16, c * 8 + 2 * e + 1);
+          best = k0 > best ? k0 : best;
+          best = k1 > best ? k1 : best;
+        }
       }
     }
     for (int64_t i = V / 8 * 8 + threadIdx.x; i < V; i += kArgmaxThreads) {
