@@ -744,8 +744,10 @@ def reference_harness_decode(device, prompt_len: int = 512, new_tokens: int = 12
 def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> dict:
     """One Qwen2-1.5B MLP (gate/up/down) at M = 4096 tokens through
     parallel.ColumnParallelMLP: unsplit on one GPU (N = 1, no collectives),
-    or split over the ranks in both modes (column: two all-gathers;
-    column_row: one all-reduce). Time is the max over ranks of CUDA-event
+    or split over the ranks in every mode (column: two all-gathers;
+    column_row: one all-reduce; column_fused: the intermediate's gather fused
+    into the SwiGLU pass as peer stores + an epoch flag wait, then one
+    all-gather of the bf16 output). Time is the max over ranks of CUDA-event
     time per forward; every output is checked against the unsplit MLP
     computed on the same rank."""
     par = importlib.import_module(PACKAGE + ".parallel")
@@ -786,8 +788,11 @@ def split_prefill(device, dist, world: int, m: int = 4096, reps: int = 10) -> di
                     "check_vs_unsplit": {"cosine": cos, "max_abs_err": err,
                                          "ok": bool(cos > 0.99999 and err <= 2e-2 + 2 ** -7 * float(ref.abs().max()))},
                     "collectives": {"column": "2 x all_gather_into_tensor (FP32 intermediate, bf16 output)",
-                                    "column_row": "1 x all_reduce (FP32 output partial sums)"}.get(mode)
+                                    "column_row": "1 x all_reduce (FP32 output partial sums)",
+                                    "column_fused": "FP32 intermediate: peer stores from the SwiGLU pass (CUDA IPC) "
+                                                    "+ bounded epoch-flag wait; bf16 output: 1 x all_gather"}.get(mode)
                     if world > 1 else "none (one GPU)"}
+        split.close()
     return out
 
 

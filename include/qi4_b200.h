@@ -159,6 +159,55 @@ QI4_API int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_
                                    const uint8_t* zeros_up, float* out, int64_t N, void* stream);
 
 /*
+ * Column-split MLP over the GPUs of one node, the gather fused into the
+ * SwiGLU pass. Replaces, for a rank's share of gate/up (output features
+ * [col0, col0 + N) of the MLP's intermediate), the fused call above followed
+ * by an all-gather of the FP32 intermediate (reference
+ * src/qwen_int4/model.py:133-135 run with gate/up split by output features
+ * over `world` ranks): the values, the same as qi4_w4g64_gate_up_silu's
+ * (the projections rounded to the activation dtype first, then silu(g) * u
+ * in FP32), are stored at outs[p][m * ld + col0 + n] for EVERY rank p - this
+ * rank's own buffer and its peers' (device pointers valid on this GPU, e.g.
+ * from qi4_ipc_open) - as they are produced. When every store of the call is
+ * done, slot `rank` of every rank's flag array (flags[p], world + 1
+ * zero-initialised 32-bit words: world flags, then that rank's CTA counter)
+ * receives `epoch` with a system-scope release store. A consumer runs
+ * qi4_peer_flag_wait on its own flag array with the same epoch before it
+ * reads its gathered buffer. Epochs increase by one per call (wrapping
+ * comparison). The caller keeps calls apart: a rank must not store into a
+ * peer's buffer while that peer still reads the previous call's contents
+ * (a collective that every rank passes after consuming, e.g. the gather of
+ * the down_proj output, does it). N may be 0 (the epoch is still published).
+ * world <= 8. Only plain stores reach peer memory (no TMA, no multicast).
+ * No reference counterpart as a single call.
+ */
+QI4_API int qi4_w4g64_gate_up_silu_scatter(const void* x, int x_dtype, int64_t M, int64_t K,
+                                           const uint8_t* qweight_gate, const uint16_t* scales_gate_f16,
+                                           const uint8_t* zeros_gate, const uint8_t* qweight_up,
+                                           const uint16_t* scales_up_f16, const uint8_t* zeros_up, int64_t N,
+                                           float* const* outs, int64_t ld, int64_t col0, uint32_t* const* flags,
+                                           int world, int rank, uint32_t epoch, void* stream);
+
+/* Waits on the GPU (one small kernel on `stream`) until flags[r] has
+ * reached `epoch` for every r < world, polling with acquire loads. A wait
+ * longer than limit_ns (1 us .. 10 s) gives up, records
+ * QI4_DEVICE_WAIT_TIMEOUT for qi4_device_status and lets the stream go on.
+ * No reference counterpart (the all-gather it completes is NCCL's there). */
+QI4_API int qi4_peer_flag_wait(const uint32_t* flags, int world, uint32_t epoch, uint64_t limit_ns, void* stream);
+
+/* Buffers shared between the processes of one node (CUDA IPC, plain
+ * peer-to-peer mappings; no multicast objects): qi4_ipc_alloc allocates
+ * `bytes` of zeroed device memory on the current device and writes its
+ * 64-byte handle; another process opens it with qi4_ipc_open (a pointer valid
+ * on that process's current device) and unmaps it with qi4_ipc_close; the
+ * owner frees it with qi4_ipc_free. These allocate, map and synchronise. No
+ * reference counterpart. */
+QI4_API int qi4_ipc_alloc(size_t bytes, void** ptr, void* handle);
+QI4_API int qi4_ipc_open(const void* handle, void** ptr);
+QI4_API int qi4_ipc_close(void* ptr);
+QI4_API int qi4_ipc_free(void* ptr);
+
+/*
  * Persistent decode chain (M <= 8 tokens): a fixed sequence of W4G64 linear
  * stages in which stage s + 1 reads what stage s (or an earlier stage)
  * wrote, run as ONE cooperative launch with one CTA per SM. It replaces a

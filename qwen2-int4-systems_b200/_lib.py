@@ -31,6 +31,13 @@ SIGNATURES = {
     "qi4_gemm_tc_plan_override": [_i, _i],
     "qi4_w4g64_linear_multi": [_p, _i, _i64, _i64, _i, _p, _p, _p, _p, _i, _p, _p, _p],
     "qi4_w4g64_gate_up_silu": [_p, _i, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _p],
+    "qi4_w4g64_gate_up_silu_scatter": [_p, _i, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _p, _i,
+                                       _i, ctypes.c_uint32, _p],
+    "qi4_peer_flag_wait": [_p, _i, ctypes.c_uint32, ctypes.c_uint64, _p],
+    "qi4_ipc_alloc": [_sz, _p, _p],
+    "qi4_ipc_open": [_p, _p],
+    "qi4_ipc_close": [_p],
+    "qi4_ipc_free": [_p],
     "qi4_gemv_mma_plan": [_i64, _i64, _i64, _i, _i, _p],
     "qi4_device_status": [_p],
     "qi4_selftest_bounded_wait": [ctypes.c_uint64, _p],

@@ -34,7 +34,7 @@ EXPORTS = [
     "qi4_w4g64_linear", "qi4_w4g64_linear_ex", "qi4_w4g64_dequant_f32",
     "qi4_w4_unpack", "qi4_w4g64_linear_f32_noalloc", "qi4_gemv_plan_override", "qi4_gemv_mma_plan_override", "qi4_gemm_tc_plan_override", "qi4_gemv_mma_plan", "qi4_w4g64_linear_multi", "qi4_w4g64_gate_up_silu", "qi4_device_status", "qi4_selftest_bounded_wait",
     "qi4_chain_create", "qi4_chain_run", "qi4_chain_info", "qi4_chain_destroy", "qi4_gqa_decode_attention", "qi4_bf16_gemv_argmax", "qi4_add_rmsnorm",
-    "qi4_w4g64_linear_multi_norm", "qi4_w4g64_gate_up_silu_norm", "qi4_gqa_decode_attention_workspace", "qi4_gqa_decode_attention_ex", "qi4_bf16_gemv_argmax_ws", "qi4_bf16_argmax_rows", "qi4_last_error", "qi4_version",
+    "qi4_w4g64_linear_multi_norm", "qi4_w4g64_gate_up_silu_norm", "qi4_gqa_decode_attention_workspace", "qi4_gqa_decode_attention_ex", "qi4_bf16_gemv_argmax_ws", "qi4_bf16_argmax_rows", "qi4_w4g64_gate_up_silu_scatter", "qi4_peer_flag_wait", "qi4_ipc_alloc", "qi4_ipc_open", "qi4_ipc_close", "qi4_ipc_free", "qi4_last_error", "qi4_version",
 ]
 
 

@@ -1,7 +1,10 @@
 // extern "C" boundary of libqi4_b200.so (declared in include/qi4_b200.h).
 //
 // Validates arguments, checks the device, picks a kernel and launches it on
-// the caller's stream. Nothing here allocates device memory or synchronises.
+// the caller's stream. Device scratch comes from the library's stream-ordered
+// pool; the qi4_ipc_* helpers (shared buffers of the multi-GPU exchange) are
+// the only entry points that allocate, map or free device memory directly,
+// and they synchronise.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -12,6 +15,7 @@
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "gemv_mma.cuh"
+#include "peer_exchange.cuh"
 #include "qi4_common.cuh"
 
 namespace qi4 {
@@ -388,11 +392,179 @@ static int gate_up_silu_impl(const void* x, int x_dtype, int64_t M, int64_t K, c
   return rc;
 }
 
+// The shard's gate/up SwiGLU stored into every rank's gathered buffer
+// (peer_exchange.cu), then the epoch published on every rank's flags.
+static int gate_up_silu_scatter_impl(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qw_gate,
+                                     const uint16_t* sc_gate, const uint8_t* z_gate, const uint8_t* qw_up,
+                                     const uint16_t* sc_up, const uint8_t* z_up, int64_t N, float* const* outs,
+                                     int64_t ld, int64_t col0, uint32_t* const* flags, int world, int rank,
+                                     uint32_t epoch, void* stream_ptr) {
+  clear_error();
+  if (!outs || !flags || world < 1 || world > kMaxPeers || rank < 0 || rank >= world) {
+    set_error("outs and flags must be host arrays of `world` device pointers, 1 <= world <= %d, 0 <= rank < world "
+              "(got world=%d rank=%d)", kMaxPeers, world, rank);
+    return QI4_ERR_ARGUMENT;
+  }
+  if (ld <= 0 || col0 < 0 || N < 0 || col0 + N > ld) {
+    set_error("the shard's columns [col0, col0 + N) = [%lld, %lld) must lie within the row pitch ld=%lld",
+              (long long)col0, (long long)(col0 + N), (long long)ld);
+    return QI4_ERR_SHAPE;
+  }
+  PeerTargets t{};
+  for (int p = 0; p < world; ++p) {
+    if (!outs[p] || !flags[p] || !aligned(outs[p], 4) || !aligned(flags[p], 4)) {
+      set_error("outs[%d] and flags[%d] must be non-null and 4-byte aligned", p, p);
+      return QI4_ERR_ARGUMENT;
+    }
+    t.out[p] = outs[p];
+    t.flags[p] = flags[p];
+  }
+  t.counter = flags[rank] + world;
+  t.ld = ld;
+  t.col0 = col0;
+  t.world = world;
+  t.rank = rank;
+  t.epoch = epoch;
+  DeviceInfo info;
+  int rc = current_device(info);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (N == 0) {  // an empty shard still publishes its epoch
+    if (!x || M <= 0) {
+      set_error("x must be non-null and M positive");
+      return QI4_ERR_ARGUMENT;
+    }
+    return check_launch(launch_swiglu_scatter(x, x, x_dtype, t, M, 0, stream, info.sms), "SwiGLU scatter");
+  }
+  rc = validate_linear(x, x_dtype, M, K, qw_gate, sc_gate, nullptr, QI4_DTYPE_NONE, outs[rank], N);
+  if (!rc) rc = validate_linear(x, x_dtype, M, K, qw_up, sc_up, nullptr, QI4_DTYPE_NONE, outs[rank], N);
+  if (rc) return rc;
+  const uint8_t* qws[2] = {qw_gate, qw_up};
+  const uint16_t* scs[2] = {sc_gate, sc_up};
+  const uint8_t* zs[2] = {z_gate, z_up};
+  // gate and up of the shard into scratch, in the activation dtype (what the
+  // reference's QuantLinear returns), then the scatter pass.
+  const size_t xsize = x_dtype == QI4_DTYPE_F32 ? 4 : 2;
+  const size_t half = ((size_t)M * (size_t)N * xsize + 255) / 256 * 256;
+  void* scratch = nullptr;
+  if (scratch_alloc(&scratch, 2 * half, stream) != cudaSuccess) {
+    set_error("scratch allocation of %zu bytes failed", 2 * half);
+    return QI4_ERR_DEVICE;
+  }
+  void* g = scratch;
+  void* u = static_cast<char*>(scratch) + half;
+  void* gu[2] = {g, u};
+  const int64_t Ns[2] = {N, N};
+  if (M > kGemvMaxM) {
+    rc = check_launch(launch_gemm_tc_multi(x, x_dtype, M, K, 2, qws, scs, zs, nullptr, QI4_DTYPE_NONE, gu, Ns, stream,
+                                           true, info.sms),
+                      "w4g64 gate/up tensor-core GEMM");
+  } else {
+    const void* bs[3] = {nullptr, nullptr, nullptr};
+    const MmaGemvPlan plan = plan_gemv_mma(M, 2 * ((N + 15) / 16 * 16), K, x_dtype, info.sms);
+    if (plan.rows == 0) {
+      set_error("no GEMV launch shape fits N=%lld K=%lld", (long long)N, (long long)K);
+      rc = QI4_ERR_SHAPE;
+    } else {
+      rc = check_launch(launch_gemv_mma_multi(x, x_dtype, M, K, 2, qws, scs, zs, bs, QI4_DTYPE_NONE, gu, Ns, stream,
+                                              true, plan, nullptr),
+                        "w4g64 gate/up GEMV");
+    }
+  }
+  if (!rc) rc = check_launch(launch_swiglu_scatter(g, u, x_dtype, t, M, N, stream, info.sms), "SwiGLU scatter");
+  scratch_free(scratch, stream);
+  return rc;
+}
+
 }  // namespace qi4
 
 using namespace qi4;
 
 extern "C" {
+
+int qi4_w4g64_gate_up_silu_scatter(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight_gate,
+                                   const uint16_t* scales_gate_f16, const uint8_t* zeros_gate,
+                                   const uint8_t* qweight_up, const uint16_t* scales_up_f16, const uint8_t* zeros_up,
+                                   int64_t N, float* const* outs, int64_t ld, int64_t col0, uint32_t* const* flags,
+                                   int world, int rank, uint32_t epoch, void* stream) {
+  return gate_up_silu_scatter_impl(x, x_dtype, M, K, qweight_gate, scales_gate_f16, zeros_gate, qweight_up,
+                                   scales_up_f16, zeros_up, N, outs, ld, col0, flags, world, rank, epoch, stream);
+}
+
+int qi4_peer_flag_wait(const uint32_t* flags, int world, uint32_t epoch, uint64_t limit_ns, void* stream) {
+  clear_error();
+  if (!flags || world < 1 || world > kMaxPeers || limit_ns < 1000 || limit_ns > 10000000000ull) {
+    set_error("flags must be non-null, 1 <= world <= %d and limit_ns in [1 us, 10 s]", kMaxPeers);
+    return QI4_ERR_ARGUMENT;
+  }
+  DeviceInfo info;
+  const int rc = current_device(info);
+  if (rc) return rc;
+  return check_launch(launch_flag_wait(flags, world, epoch, limit_ns, static_cast<cudaStream_t>(stream)),
+                      "peer flag wait");
+}
+
+int qi4_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  clear_error();
+  if (!ptr || !handle || bytes == 0) {
+    set_error("ptr and handle must be non-null and bytes positive");
+    return QI4_ERR_ARGUMENT;
+  }
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    cudaGetLastError();
+    set_error("IPC buffer of %zu bytes: %s", bytes, cudaGetErrorString(e));
+    return QI4_ERR_DEVICE;
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return QI4_OK;
+}
+
+int qi4_ipc_open(const void* handle, void** ptr) {
+  clear_error();
+  if (!ptr || !handle) {
+    set_error("handle and ptr must be non-null");
+    return QI4_ERR_ARGUMENT;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    return QI4_ERR_DEVICE;
+  }
+  return QI4_OK;
+}
+
+int qi4_ipc_close(void* ptr) {
+  clear_error();
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+    return QI4_ERR_DEVICE;
+  }
+  return QI4_OK;
+}
+
+int qi4_ipc_free(void* ptr) {
+  clear_error();
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaFree: %s", cudaGetErrorString(e));
+    return QI4_ERR_DEVICE;
+  }
+  return QI4_OK;
+}
 
 int qi4_w4g64_gate_up_silu(const void* x, int x_dtype, int64_t M, int64_t K, const uint8_t* qweight_gate,
                            const uint16_t* scales_gate_f16, const uint8_t* zeros_gate, const uint8_t* qweight_up,
@@ -576,7 +748,8 @@ int qi4_device_status(void* stream) {
   const int v2 = read_gemm_tc_error(static_cast<cudaStream_t>(stream));
   const int v3 = read_chain_error(static_cast<cudaStream_t>(stream));
   const int v4 = read_attention_error(static_cast<cudaStream_t>(stream));
-  const int v = (v1 < 0 || v2 < 0 || v3 < 0 || v4 < 0) ? -1 : (v1 | v2 | v3 | v4);
+  const int v5 = read_peer_error(static_cast<cudaStream_t>(stream));
+  const int v = (v1 < 0 || v2 < 0 || v3 < 0 || v4 < 0 || v5 < 0) ? -1 : (v1 | v2 | v3 | v4 | v5);
   if (v < 0) {
     set_error("cannot read the device error flags: %s", cudaGetErrorString(cudaGetLastError()));
     return QI4_ERR_LAUNCH;

@@ -15,7 +15,11 @@ gate and up shards line up element-wise, so ``silu(gate) * up`` is formed on
 the shard by the fused gate/up call; ``ColumnParallelMLP`` then either
 gathers it for a column-split ``down_proj`` (two all-gathers per MLP) or
 feeds it to a ``down_proj`` split by input features on the same boundaries
-(one all-reduce of the output, the intermediate never leaves the GPU).
+(one all-reduce of the output, the intermediate never leaves the GPU), or, in
+``column_fused`` mode, has the SwiGLU pass store its shard straight into
+every rank's gathered intermediate over CUDA IPC peer mappings and publish a
+per-call epoch flag (``qi4_w4g64_gate_up_silu_scatter``), which each rank
+waits for on the GPU (``qi4_peer_flag_wait``) before its ``down_proj``.
 
 The per-shard compute is pluggable (``linear_fn``) so that the sharding and
 gathering logic can be tested on CPU ranks (gloo) against the oracle; the
@@ -24,6 +28,7 @@ default is the CUDA backend, with no CPU fallback.
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable
 
@@ -145,6 +150,59 @@ def gather_columns(local: torch.Tensor, n_total: int, group=None, bounds=None) -
     return out
 
 
+class _DevArray:
+    """A device buffer given as a raw pointer, viewable as a torch tensor."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerGatherBuffers:
+    """Every rank's gathered FP32 intermediate [rows, width] and its flag words
+    (world flags + one CTA counter), in one buffer per rank shared over CUDA
+    IPC (plain peer mappings, no multicast); with one process, a local buffer.
+    Collective: every rank of ``group`` constructs it with the same sizes."""
+
+    def __init__(self, lib, rows: int, width: int, group, device):
+        from . import _lib
+
+        self.lib, self.rows, self.width = lib, rows, width
+        self.world, self.rank = _world(group)
+        data_bytes = (rows * width * 4 + 255) // 256 * 256
+        total = data_bytes + 256
+        self._opened, self._owned, self._tensor = [], None, None
+        if self.world == 1:
+            self._tensor = torch.zeros(total // 4, dtype=torch.float32, device=device)
+            bases = [self._tensor.data_ptr()]
+        else:
+            ptr, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+            _lib.check(lib.qi4_ipc_alloc(total, ctypes.byref(ptr), handle), "qi4_ipc_alloc")
+            self._owned = ptr.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            bases = []
+            for p, h in enumerate(handles):
+                if p == self.rank:
+                    bases.append(self._owned)
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(lib.qi4_ipc_open((ctypes.c_char * 64).from_buffer_copy(h), ctypes.byref(peer)),
+                           "qi4_ipc_open")
+                self._opened.append(peer.value)
+                bases.append(peer.value)
+        self.data = [b for b in bases]
+        self.flags = [b + data_bytes for b in bases]
+        self.local = torch.as_tensor(_DevArray(self.data[self.rank], (rows, width)), device=device)
+
+    def close(self):
+        for p in self._opened:
+            self.lib.qi4_ipc_close(p)
+        if self._owned is not None:
+            self.lib.qi4_ipc_free(self._owned)
+        self._opened, self._owned, self._tensor = [], None, None
+
+
 class ColumnParallelW4G64:
     """One W4G64 linear split by output features over the ranks of ``group``."""
 
@@ -188,13 +246,22 @@ class ColumnParallelMLP:
       all-reduce (M x 1536 FP32) and cast. Nothing of the intermediate
       crosses the link. The sum over ranks changes the FP32 summation order
       only.
+    * ``"column_fused"`` - as ``"column"``, but the intermediate's gather is
+      fused into the SwiGLU pass: each value is stored into every rank's
+      gathered buffer (peer stores over NVLink) as it is produced, and a
+      per-call epoch flag, waited for on the GPU with a time limit
+      (``flag_timeout_s``; a time-out is reported by ``qi4_device_status``),
+      replaces the collective. The down_proj output is gathered over NCCL,
+      which also keeps a rank from overwriting a peer's intermediate before
+      that peer's down_proj has read it. CUDA backend only.
 
     With one process (no process group) both modes are the unsplit MLP.
     """
 
-    MODES = ("column", "column_row")
+    MODES = ("column", "column_row", "column_fused")
 
-    def __init__(self, mlp, group=None, linear_fn=None, mode: str = "column", swiglu_fn=None):
+    def __init__(self, mlp, group=None, linear_fn=None, mode: str = "column", swiglu_fn=None,
+                 flag_timeout_s: float = 2.0):
         if mode not in self.MODES:
             raise ValueError(f"mode must be one of {self.MODES}, got {mode!r}")
         self.group, self.mode = group, mode
@@ -205,7 +272,12 @@ class ColumnParallelMLP:
         a, b = self.bounds[self.rank]
         self.gate = shard_rows(gate.qweight, gate.scales, gate.zeros, None, in_features=self.hidden, start=a, stop=b)
         self.up = shard_rows(up.qweight, up.scales, up.zeros, None, in_features=self.hidden, start=a, stop=b)
-        if mode == "column":
+        if mode == "column_fused" and (linear_fn is not None or swiglu_fn is not None
+                                       or gate.qweight.device.type != "cuda"):
+            raise ValueError("mode 'column_fused' runs the CUDA kernels only (no linear_fn / swiglu_fn, CUDA weights)")
+        self.flag_timeout_ns = int(flag_timeout_s * 1e9)
+        self._peer, self._epoch = None, 0
+        if mode in ("column", "column_fused"):
             ra, rb = shard_bounds(self.hidden, self.world, self.rank)
             self.down = shard_rows(down.qweight, down.scales, down.zeros, down.bias, in_features=self.inter,
                                    start=ra, stop=rb)
@@ -219,9 +291,47 @@ class ColumnParallelMLP:
                                          * self.linear_fn(x, u).float())
         self.swiglu_fn = swiglu_fn or _default_swiglu
 
+    def _fused_intermediate(self, x2: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+
+        lib = _lib.load()
+        m = x2.shape[0]
+        if self._peer is None or self._peer.rows < m:  # collective: every rank sees the same M
+            if self._peer is not None:
+                self.close()
+            self._peer = PeerGatherBuffers(lib, m, self.inter, self.group, x2.device)
+            self._epoch = 0
+        self._epoch = (self._epoch + 1) & 0xFFFFFFFF
+        pb, w = self._peer, self.world
+        codes = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+        x2 = x2.contiguous()
+        g, u = self.gate, self.up
+        stream = torch.cuda.current_stream(x2.device).cuda_stream
+        rc = lib.qi4_w4g64_gate_up_silu_scatter(
+            x2.data_ptr(), codes[x2.dtype], m, self.hidden, g.qweight.data_ptr(), g.scales.data_ptr(),
+            g.zeros.data_ptr(), u.qweight.data_ptr(), u.scales.data_ptr(), u.zeros.data_ptr(), g.out_features,
+            (ctypes.c_void_p * w)(*pb.data), self.inter, self.bounds[self.rank][0], (ctypes.c_void_p * w)(*pb.flags),
+            w, self.rank, self._epoch, stream)
+        _lib.check(rc, "qi4_w4g64_gate_up_silu_scatter")
+        _lib.check(lib.qi4_peer_flag_wait(pb.flags[self.rank], w, self._epoch, self.flag_timeout_ns, stream),
+                   "qi4_peer_flag_wait")
+        return pb.local[:m]
+
+    def close(self):
+        """Releases the peer buffers of ``column_fused`` mode (collective)."""
+        if self._peer is not None:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)  # no peer still stores into or reads these buffers
+            self._peer.close()
+            self._peer = None
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.hidden)
+        if self.mode == "column_fused":
+            y = self.linear_fn(self._fused_intermediate(x2), self.down).to(x.dtype)
+            return gather_columns(y, self.hidden, self.group).reshape(*lead, self.hidden)
         if self.gate.out_features:
             h = self.swiglu_fn(x2, self.gate, self.up)
         else:

@@ -1,7 +1,10 @@
 """Column-split W4G64 on 2 GPUs over NCCL (skipped on a single-GPU host).
 
-A split linear against the oracle, and the Qwen2 MLP in both split modes
-against the same MLP unsplit on one GPU (the b200 kernels either way).
+A split linear against the oracle, and the Qwen2 MLP in the three split
+modes (two NCCL collectives; one all-reduce; the intermediate's gather fused
+into the SwiGLU pass over CUDA IPC peer memory, called twice on the same
+buffers) against the same MLP unsplit on one GPU (the b200 kernels either
+way).
 """
 
 import datetime
@@ -66,10 +69,21 @@ def _worker(rank, world, port, result_path):
         d = mlp.down_proj
         ref = b200.b200_w4g64_linear(hm, d.qweight, d.scales, d.zeros, None, out_features=1536, in_features=8960,
                                      group_size=64, packing="canonical").to(torch.bfloat16).float()
-        for mode in ("column", "column_row"):
-            got = par.ColumnParallelMLP(mlp, mode=mode)(x).float()
+        for mode in ("column", "column_row", "column_fused"):
+            split = par.ColumnParallelMLP(mlp, mode=mode)
+            got = split(x).float()
             cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0)
             ok = ok and bool((got - ref).abs().max() <= 2e-2 + 2 ** -7 * ref.abs().max()) and float(cos) > 0.99999
+            if mode == "column_fused":
+                # A second call reuses the peer buffers with the next epoch;
+                # a shorter input reuses them too.
+                x2 = torch.flip(x, dims=(0,))[:300].contiguous()
+                ref2 = torch.flip(ref, dims=(0,))[:300]
+                got2 = split(x2).float()
+                ok = ok and bool((got2 - ref2).abs().max() <= 2e-2 + 2 ** -7 * ref2.abs().max())
+                lib = importlib.import_module("qwen2-int4-systems_b200._lib").load()
+                ok = ok and lib.qi4_device_status(torch.cuda.current_stream().cuda_stream) == 0
+                split.close()
         flag = torch.tensor([1 if ok else 0], device=dev)
         dist.all_reduce(flag, op=dist.ReduceOp.MIN)
         if rank == 0:
