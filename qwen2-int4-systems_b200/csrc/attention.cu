@@ -30,6 +30,8 @@
 // partial (max, sum, 128 sums per head) goes to scratch; a second kernel
 // combines the splits per head. Both launch as programmatic
 // dependents (the next kernel's prologue overlaps this one's tail).
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cmath>
 
@@ -45,6 +47,7 @@ constexpr int kD = 128;          // head dim
 constexpr int kMaxGroup = 8;     // query heads per KV head
 constexpr int kSplitKeys = 64;   // keys per CTA
 constexpr int kWarps = 4;        // per CTA: 16 keys of the split each
+constexpr int kMaxClusterSplits = 16;  // splits merged inside one cluster (non-portable size above 8)
 constexpr int kQbStride = kD + 8;  // bf16 per staged query row (conflict-free fragment loads)
 
 struct AttnArgs {
@@ -60,7 +63,8 @@ struct AttnArgs {
   const int32_t* lengths;      // [B] past length L_b (the new token goes at L_b)
   const uint8_t* key_mask;     // [B, mask_stride], or null
   int64_t mask_stride;
-  float* partial;              // [B][Hkv][splits][G][kD + 2]
+  float* partial;              // [B][Hkv][splits][G][kD + 2] (two-kernel path)
+  __nv_bfloat16* out;          // [B, Hq, D] (cluster path: written by the kernel itself)
   int B, Hq, Hkv, G, cap, splits;
   float scale;
   int early;                   // 1: lengths, positions and the past cache rows are read before the dependency wait
@@ -122,19 +126,15 @@ __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r
                : "r"(addr));
 }
 
-__global__ void __launch_bounds__(kWarps * 32, 5) gqa_decode_kernel(const AttnArgs a) {
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  // Programmatic dependent launch: the next kernel may start its prologue;
-  // this one waits for its predecessor (the q/k/v projections) before it
-  // reads q / k_new / v_new - and, unless the caller vouched that lengths and
-  // the past cache rows are not written by the launches just before this one
-  // (`early`), before anything at all.
-  pdl_launch_dependents();
-  if (!a.early) pdl_wait();
-  const int L = a.lengths[b];  // past keys; the new one is key L
+// One CTA's share: keys [split * 64, ...) of sequence b (past length L) for
+// the G query heads of KV head kvh, appended key / value included; its
+// partial (per head: max, sum, 128 weighted sums) goes to `out`
+// ([G][kD + 2] floats, global or shared memory). Called with keys present
+// and room in the cache.
+__device__ __forceinline__ void attend_split(const AttnArgs& a, const int split, const int kvh, const int b,
+                                             const int L, float* __restrict__ out) {
   const int nkeys = L + 1;
   const int k0 = split * kSplitKeys;
-  if (k0 >= nkeys || L >= a.cap) return;  // nothing of this sequence here (or no room)
   const int k1 = min(nkeys, k0 + kSplitKeys);
   const int G = a.G;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -318,7 +318,6 @@ __global__ void __launch_bounds__(kWarps * 32, 5) gqa_decode_kernel(const AttnAr
   __syncthreads();
   // Combine the warps into the CTA's partial (warps without keys have m = -inf):
   // per head the running max, each warp's weight e^(m_w - max) and the sum.
-  float* out = a.partial + (((int64_t)b * a.Hkv + kvh) * a.splits + split) * G * (kD + 2);
   if (tid < G) {
     const int h = tid;
     float mm = -INFINITY;
@@ -341,6 +340,65 @@ __global__ void __launch_bounds__(kWarps * 32, 5) gqa_decode_kernel(const AttnAr
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) as += red_acc[w][h][d] * red_f[w][h];
     out[h * (kD + 2) + 2 + d] = as;
+  }
+}
+
+// kCluster = false: one CTA per (split, KV head, sequence) writes its partial
+// to the workspace; gqa_combine_kernel merges the splits. kCluster = true
+// (grids whose splits fit one thread-block cluster): the splits of a
+// (sequence, KV head) are one cluster, the partials stay in shared memory,
+// and after a cluster barrier CTA r merges heads r, r + C, ... over
+// distributed shared memory - the combine kernel's arithmetic in the same
+// order, so the output is bit-identical - and writes the bf16 output. CTAs
+// without keys still take both cluster barriers.
+template <bool kCluster>
+__global__ void __launch_bounds__(kWarps * 32, 5) gqa_decode_kernel(const AttnArgs a) {
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // Programmatic dependent launch: the next kernel may start its prologue;
+  // this one waits for its predecessor (the q/k/v projections) before it
+  // reads q / k_new / v_new - and, unless the caller vouched that lengths and
+  // the past cache rows are not written by the launches just before this one
+  // (`early`), before anything at all.
+  pdl_launch_dependents();
+  if (!a.early) pdl_wait();
+  const int L = a.lengths[b];  // past keys; the new one is key L
+  const bool active = split * kSplitKeys < L + 1 && L < a.cap;  // keys of this sequence here, and room
+  if constexpr (!kCluster) {
+    if (!active) return;
+    attend_split(a, split, kvh, b, L,
+                 a.partial + (((int64_t)b * a.Hkv + kvh) * a.splits + split) * a.G * (kD + 2));
+  } else {
+    __shared__ __align__(16) float part_s[kMaxGroup][kD + 2];
+    if (active) attend_split(a, split, kvh, b, L, &part_s[0][0]);
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every partial of this (sequence, KV head) is written
+    // The output may be read by a launch before the predecessor until that
+    // one is done: write it only after the dependency wait.
+    pdl_wait();
+    const int G = a.G, C = (int)cluster.num_blocks(), r = (int)cluster.block_rank();
+    const int d = threadIdx.x;  // blockDim = kD: one output dimension per thread
+    const int used = L < a.cap ? min(C, (L + 1 + kSplitKeys - 1) / kSplitKeys) : 0;
+    for (int hg = r; hg < G; hg += C) {
+      __nv_bfloat16* o = a.out + ((int64_t)b * a.Hq + kvh * G + hg) * kD;
+      if (L >= a.cap) {
+        o[d] = __float2bfloat16_rn(0.f);
+        if (d == 0 && kvh == 0 && hg == 0) atomicOr(&g_attention_error, 2);
+        continue;
+      }
+      float M = -INFINITY;
+      for (int sp = 0; sp < used; ++sp) M = fmaxf(M, cluster.map_shared_rank(&part_s[hg][0], sp)[0]);
+      float num = 0.f, den = 0.f;
+      for (int sp = 0; sp < used; ++sp) {
+        const float* p = cluster.map_shared_rank(&part_s[hg][0], sp);
+        const float m = p[0];
+        const float f = m == -INFINITY ? 0.f : __expf(m - M);
+        num += p[2 + d] * f;
+        den += p[1] * f;
+      }
+      o[d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    }
+    cluster.sync();  // no CTA leaves while a peer still reads its partial
   }
 }
 
@@ -426,6 +484,7 @@ cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_ne
   a.key_mask = key_mask;
   a.mask_stride = mask_stride;
   a.partial = partial;
+  a.out = static_cast<__nv_bfloat16*>(out);
   a.B = B;
   a.Hq = Hq;
   a.Hkv = Hkv;
@@ -442,7 +501,31 @@ cudaError_t launch_gqa_decode(const void* q, const void* k_new, const void* v_ne
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_decode_kernel, a);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Small grids (their time is one CTA's serial path): the splits of a
+  // (sequence, KV head) as one cluster, merged in the kernel - no combine
+  // launch. Up to 16 splits (1024 keys of capacity).
+  if (a.splits <= kMaxClusterSplits && (int64_t)a.splits * Hkv * B <= 2 * (int64_t)sms) {
+    static unsigned long long configured = 0;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (!(configured & bit)) {
+      cudaError_t e = cudaFuncSetAttribute(gqa_decode_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+      configured |= bit;
+    }
+    cudaLaunchAttribute cattr[2];
+    cattr[0] = attr[0];
+    cattr[1].id = cudaLaunchAttributeClusterDimension;
+    cattr[1].val.clusterDim.x = (unsigned)a.splits;
+    cattr[1].val.clusterDim.y = 1;
+    cattr[1].val.clusterDim.z = 1;
+    cfg.attrs = cattr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, gqa_decode_kernel<true>, a);
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gqa_decode_kernel<false>, a);
   if (e != cudaSuccess) return e;
   cfg.gridDim = dim3(Hq, B, 1);
   cfg.blockDim = dim3(kD, 1, 1);

@@ -176,3 +176,46 @@ def test_workspace_and_early_cache_read_give_the_same_result(b200, cuda_device):
         outs.append((out, kc, vc))
     for out, kc, vc in outs[1:]:
         assert torch.equal(out, outs[0][0]) and torch.equal(kc, outs[0][1]) and torch.equal(vc, outs[0][2])
+
+
+@pytest.mark.parametrize(("cap", "lengths", "big"), [(1000, [998, 300, 0, 1000], 10), (100, [99, 64, 63, 7], 80)])
+def test_cluster_merge_equals_the_combine_kernel(b200, cuda_device, cap, lengths, big):
+    """Small grids merge the splits of a (sequence, KV head) inside one
+    thread-block cluster (no combine launch); large grids use the combine
+    kernel. The same sequences, alone (cluster path: 16 or 2 splits, so one
+    or three heads per merging CTA) and as the first rows of a batch large
+    enough for the two-kernel path, give bit-identical outputs and caches; a
+    full cache gives zeros and QI4_DEVICE_CACHE_FULL on both paths; splits
+    without keys (short sequences) still take part in the cluster."""
+    lm = importlib.import_module(b200.__name__ + "._lib")
+    lib = lm.load()
+    g = torch.Generator(device="cpu").manual_seed(cap)
+    Hq, Hkv, D = 12, 2, 128
+    bf = dict(dtype=torch.bfloat16, device=cuda_device)
+    q = torch.randn(big, Hq, D, generator=g).to(**bf)
+    kn, vn = torch.randn(big, Hkv, D, generator=g).to(**bf), torch.randn(big, Hkv, D, generator=g).to(**bf)
+    kc0, vc0 = torch.randn(big, Hkv, cap, D, generator=g).to(**bf), torch.randn(big, Hkv, cap, D, generator=g).to(**bf)
+    small = len(lengths)
+    lens = torch.tensor(lengths + [cap // 2] * (big - small), dtype=torch.int32, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    full = any(x >= cap for x in lengths)
+    res = []
+    for B in (small, big):
+        kc, vc = kc0[:B].clone(), vc0[:B].clone()
+        out = torch.full((B, Hq * D), float("nan"), **bf)
+        n = lib.qi4_gqa_decode_attention_workspace(B, Hq, Hkv, cap)
+        ws = torch.empty(n, dtype=torch.uint8, device=cuda_device)
+        rc = lib.qi4_gqa_decode_attention_ex(
+            q.data_ptr(), kn.data_ptr(), vn.data_ptr(), None, None, None, kc.data_ptr(), vc.data_ptr(), kc.stride(0),
+            kc.stride(1), cap, lens.data_ptr(), None, 0, out.data_ptr(), B, Hq, Hkv, D, ctypes.c_float(D ** -0.5), 0,
+            ws.data_ptr(), n, s)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert lib.qi4_device_status(s) == (2 if full else 0)
+        res.append((out[:small], kc[:small], vc[:small]))
+    (o1, k1, v1), (o2, k2, v2) = res
+    assert not bool(o1.isnan().any())
+    assert torch.equal(o1, o2) and torch.equal(k1, k2) and torch.equal(v1, v2)
+    for i, L in enumerate(lengths):
+        if L >= cap:
+            assert bool((o1[i] == 0).all())
