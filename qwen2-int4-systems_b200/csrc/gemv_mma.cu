@@ -312,17 +312,52 @@ __device__ __forceinline__ void stage_x_norm(const Args& a, uint8_t* xs, int xst
   const NormPrologue& nm = a.norm;
   const int K = (int)a.K, chunks = K / 8;
   const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
-  for (int tok = warp; tok < a.M; tok += nw) {
-    float ss = 0.f;
-    for (int c = lane; c < chunks; c += 32) {
-      float v[8];
-      residual8(nm, (int64_t)tok * K + c * 8, v);
+  // Sum of squares per token. Up to 4 tokens: the whole CTA works on every
+  // token (each thread a share of the row's 8-element chunks, the loads of
+  // all tokens in flight at once), then per warp by shuffles and over the
+  // warps in order - one warp per token would walk the row alone, a chain of
+  // dependent L2 round trips. More tokens: one warp per token, the warps
+  // working on different tokens at once.
+  constexpr int kTokAll = 4;
+  if (a.M <= kTokAll) {
+    __shared__ float red[kTokAll][32];  // [token][warp]
+    float ss[kTokAll] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = tid; c < chunks; c += nthreads) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+      for (int t = 0; t < kTokAll; ++t) {
+        if (t < a.M) {
+          float v[8];
+          residual8(nm, (int64_t)t * K + c * 8, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss[t] = fmaf(v[j], v[j], ss[t]);
+        }
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) rs[tok] = rsqrtf(ss / (float)K + nm.eps);
+    for (int t = 0; t < kTokAll; ++t) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+      if (lane == 0) red[t][warp] = ss[t];
+    }
+    __syncthreads();
+    if (tid < a.M) {
+      float tot = 0.f;
+      for (int w = 0; w < nw; ++w) tot += red[tid][w];
+      rs[tid] = rsqrtf(tot / (float)K + nm.eps);
+    }
+  } else {
+    for (int tok = warp; tok < a.M; tok += nw) {
+      float ss = 0.f;
+      for (int c = lane; c < chunks; c += 32) {
+        float v[8];
+        residual8(nm, (int64_t)tok * K + c * 8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) rs[tok] = rsqrtf(ss / (float)K + nm.eps);
+    }
   }
   __syncthreads();
   const int per_tok = gs * 8;  // 8-element chunks of the slice per token
