@@ -10,7 +10,7 @@ library's kernels, on static buffers:
 
   embed -> per layer: residual add + RMSNorm and q/k/v in one launch
            (qi4_w4g64_linear_multi_norm: the GEMV forms its activations from
-           the residual stream while staging them; up to 16 sequences, else
+           the residual stream while staging them; up to 8 sequences, else
            qi4_add_rmsnorm + qi4_w4g64_linear_multi), RoPE + KV append + GQA
            attention (qi4_gqa_decode_attention), o_proj (qi4_w4g64_linear),
            residual add + RMSNorm and gate/up + SwiGLU in one launch
@@ -87,10 +87,12 @@ class DecodeEngine:
         # Static buffers of a step.
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         # The bf16 residual stream: with the norm folded into the next launch
-        # (up to 16 sequences) each boundary reads one buffer and writes the
-        # other; otherwise the norm kernel updates hbuf[0] in place.
+        # (up to 8 sequences: every CTA of that launch recomputes the rows'
+        # statistics, which at 16 sequences costs more than a norm launch)
+        # each boundary reads one buffer and writes the other; otherwise the
+        # norm kernel updates hbuf[0] in place.
         self.hbuf = [torch.empty(B, self.D, **bf), torch.empty(B, self.D, **bf)]
-        self.fuse_norm = B <= 16
+        self.fuse_norm = B <= 8
         self.x = torch.empty(B, self.D, **bf)
         self.q = torch.empty(B, self.Hq * self.hd, **bf)
         self.k = torch.empty(B, self.Hkv * self.hd, **bf)
