@@ -502,8 +502,10 @@ def step_variants(lib, layers, device, gen, dist) -> dict:
 
 def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
     """Secondary figures for the workloads the headline does not cover:
-    config 0 (gate, symmetric, M = 1/4/16), config 1's other M points
-    (8/32/128/512, the seven shapes of all 28 layers: 655 MB rotated, > 5x
+    config 0 (gate-shaped 1536 -> 8960, symmetric, M = 1/4/16: the 56 gate
+    and up matrices of the 28 layers, 410 MB rotated, > 3x L2), config 1's
+    other M points (8/32/128/512, the seven shapes of all 28 layers: 655 MB
+    rotated, > 5x
     L2), config 2 (AWQ-style asymmetric down_proj, M = 1/16/2048, 40 distinct
     matrices: 280 MB rotated, > 2x L2) and the 196 linears at M = 64 (the
     linear part of config 4's decode step; the whole step is under
@@ -516,7 +518,7 @@ def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
         t = time_graph(chain.graph(), reps=reps, warmup=3)
         return t, chain.bytes() / (t / 1e3) / 1e9, chain.flops() / (t / 1e3) / 1e12
 
-    gates = [layer[4] for layer in layers]
+    gates = [layer[i] for layer in layers for i in (4, 5)]  # gate and up: the same shape and format
     out["cfg0_gate_sym_GBps"] = {f"m{m}": round(run(Chain(lib, gates, m, device, gen))[1], 1) for m in (1, 4, 16)}
     sweep = {}
     everything = [e for layer in layers for e in layer]
