@@ -505,8 +505,8 @@ def config_sweep(lib, layers, device, gen, tensor_peak: float) -> dict:
     config 0 (gate-shaped 1536 -> 8960, symmetric, M = 1/4/16: the 56 gate
     and up matrices of the 28 layers, 410 MB rotated, > 3x L2), config 1's
     other M points (8/32/128/512, the seven shapes of all 28 layers: 655 MB
-    rotated, > 5x
-    L2), config 2 (AWQ-style asymmetric down_proj, M = 1/16/2048, 40 distinct
+    rotated, > 5x L2), config 2 (AWQ-style asymmetric down_proj, M =
+    1/16/2048, 40 distinct
     matrices: 280 MB rotated, > 2x L2) and the 196 linears at M = 64 (the
     linear part of config 4's decode step; the whole step is under
     ``serving``). Library-chosen kernels (GEMV up to M = 16, tensor cores
