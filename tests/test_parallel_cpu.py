@@ -167,6 +167,14 @@ def test_single_process_mlp_is_the_unsplit_mlp():
     a = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode="column")(x)
     b = par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode="column_row")(x)
     assert torch.equal(a, b)
+    # The fused exchange is the CUDA kernels' own (peer stores over CUDA IPC):
+    # CPU weights or a pluggable shard compute are refused, never emulated.
+    with pytest.raises(ValueError, match="column_fused"):
+        par.ColumnParallelMLP(mlp, mode="column_fused")
+    with pytest.raises(ValueError, match="column_fused"):
+        par.ColumnParallelMLP(mlp, linear_fn=_oracle_linear, mode="column_fused")
+    with pytest.raises(ValueError, match="mode must be one of"):
+        par.ColumnParallelMLP(mlp, mode="row")
 
 
 def test_group_bounds_and_column_shards():
