@@ -925,9 +925,15 @@ MmaGemvPlan plan_gemv_mma(int64_t M, int64_t N, int64_t K, int x_dtype, int num_
   // CTAs that get boxes, so the loops step `req`, which always terminates.
   int req = 1;
   MmaGemvPlan best = make(R, req, 8);
+  // FP32 activations stage twice the bytes per token: from 13 tokens on a
+  // split of at most 8 still needs more than 110 KB per CTA (one CTA per SM,
+  // 2.3 waves for down_proj at M = 16: 31.6 us against 17.4 us at M = 12), so
+  // their split may grow to 16 CTAs (a non-portable cluster size).
+  const int max_req = x_dtype == QI4_DTYPE_F32 ? 16 : 8;
   if (M >= 4 && nboxes >= 16) {
-    while (req < 8 && req < nboxes &&
-           (tiles * best.ksplit < (int64_t)(1.5 * num_sms) || best.smem > 110 * 1024))
+    while (req < nboxes && ((req < 8 && (tiles * best.ksplit < (int64_t)(1.5 * num_sms) ||
+                                         best.smem > 110 * 1024)) ||
+                            (req < max_req && best.smem > 110 * 1024)))
       best = make(R, ++req, 8);
   }
   while (best.smem > 200 * 1024 && req < 8 && req < nboxes) best = make(R, ++req, 8);

@@ -79,6 +79,11 @@ def test_engine_instances_in_sequence_after_prefill(b200, cuda_device):
         seqs.append(engine.generate(prompt, 8))
         engine.close()
         del engine
+    # The full model's logits here lie around 8-16, where one bf16 step is
+    # 0.0625: a position counts as clear when its top two differ by more than
+    # two steps (0.13). The reference forward rounds the dequantised weights
+    # to bf16 on its tensor-core path, so one-step ties can go either way; the
+    # stale-state failure this guards against disagreed at every position.
     for seq in seqs:
-        _check_teacher_forced(model, seq, 256)
+        _check_teacher_forced(model, seq, 256, gap=0.13)
     assert torch.equal(seqs[0], seqs[1]) and torch.equal(seqs[1], seqs[2])

@@ -210,7 +210,7 @@ def test_gemv_shape_sweep(b200, cuda_device, name, m, algo):
 
 @pytest.mark.parametrize("algo", ["gemv", "gemv_fma"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("m", [1, 16])
+@pytest.mark.parametrize("m", [1, 13, 16])
 def test_gemv_awq_down_proj_all_dtypes(b200, cuda_device, dtype, m, algo):
     qw, sc, z = G.cfg2_weights()
     chan = torch.from_numpy(G.arrays()["cfg2_chan"])
