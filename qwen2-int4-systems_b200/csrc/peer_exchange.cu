@@ -109,6 +109,21 @@ __global__ void __launch_bounds__(32) flag_wait_kernel(const uint32_t* flags, in
 
 }  // namespace
 
+namespace {
+
+template <typename T>
+void launch_scatter_t(const void* g, const void* u, const PeerTargets& t, int64_t M, int64_t n, bool vec, int blocks,
+                      cudaStream_t stream) {
+  if (vec)
+    swiglu_scatter_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(g), static_cast<const T*>(u), t,
+                                                               M, n);
+  else
+    swiglu_scatter_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(g), static_cast<const T*>(u), t,
+                                                                M, n);
+}
+
+}  // namespace
+
 cudaError_t launch_swiglu_scatter(const void* g, const void* u, int dtype, const PeerTargets& t, int64_t M, int64_t n,
                                   cudaStream_t stream, int num_sms) {
   bool vec = n % 4 == 0 && t.ld % 4 == 0 && t.col0 % 4 == 0;
@@ -116,19 +131,11 @@ cudaError_t launch_swiglu_scatter(const void* g, const void* u, int dtype, const
   const int64_t items = vec ? M * (n / 4) : M * n;
   // At least one CTA, so that the epoch is published even for an empty shard.
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, (int64_t)num_sms * 8));
-#define QI4_SCATTER(T)                                                                                          \
-  (vec ? (swiglu_scatter_kernel<T, true><<<blocks, 256, 0, stream>>>(static_cast<const T*>(g),                \
-                                                                     static_cast<const T*>(u), t, M, n),       \
-          0)                                                                                                   \
-       : (swiglu_scatter_kernel<T, false><<<blocks, 256, 0, stream>>>(static_cast<const T*>(g),               \
-                                                                      static_cast<const T*>(u), t, M, n),      \
-          0))
   switch (dtype) {
-    case QI4_DTYPE_F16: QI4_SCATTER(__half); break;
-    case QI4_DTYPE_BF16: QI4_SCATTER(__nv_bfloat16); break;
-    default: QI4_SCATTER(float); break;
+    case QI4_DTYPE_F16: launch_scatter_t<__half>(g, u, t, M, n, vec, blocks, stream); break;
+    case QI4_DTYPE_BF16: launch_scatter_t<__nv_bfloat16>(g, u, t, M, n, vec, blocks, stream); break;
+    default: launch_scatter_t<float>(g, u, t, M, n, vec, blocks, stream); break;
   }
-#undef QI4_SCATTER
   return cudaGetLastError();
 }
 
