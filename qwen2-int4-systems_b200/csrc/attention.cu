@@ -27,9 +27,12 @@
 // rows of a zero-padded 16-row operand, an online softmax on the score
 // registers, and P.V with the FP32 weights split into two bf16 parts (high
 // and remainder: the products keep 16 bits of each weight). The CTA's
-// partial (max, sum, 128 sums per head) goes to scratch; a second kernel
-// combines the splits per head. Both launch as programmatic
-// dependents (the next kernel's prologue overlaps this one's tail).
+// partial (max, sum, 128 sums per head) goes to scratch and a second kernel
+// combines the splits per head; for small grids (at most 16 splits) the
+// splits of a (sequence, KV head) form one thread-block cluster and merge
+// over distributed shared memory in the same order instead. Launches are
+// programmatic dependents (the next kernel's prologue overlaps this one's
+// tail).
 #include <cooperative_groups.h>
 
 #include <algorithm>
