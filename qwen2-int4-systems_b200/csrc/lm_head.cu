@@ -239,14 +239,25 @@ cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s
 }
 
 template <int M>
-cudaError_t launch_m(const void* w, const void* x, int64_t N, int K, void* logits, unsigned long long* keys,
-                     int grid, int64_t rows_per_cta, cudaStream_t stream) {
+cudaError_t launch_m(const void* w, const void* x, int64_t N, int K, void* logits, unsigned long long* keys, int sms,
+                     cudaStream_t stream) {
   const size_t smem = (size_t)M * K * 2;
   if (smem > 48 * 1024) {
     const cudaError_t e = cudaFuncSetAttribute(gemv_argmax_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int)smem);
     if (e != cudaSuccess) return e;
   }
+  // One wave: as many CTAs as fit on the SMs at once (registers bound it: at
+  // M = 1, 76 registers allow three 256-thread CTAs per SM), each an equal
+  // share of the rows - a fixed four per SM left a thin second wave.
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_argmax_kernel<M>, kThreads, smem) != cudaSuccess ||
+      occ < 1) {
+    cudaGetLastError();
+    occ = 1;
+  }
+  const int grid = sms * occ;
+  const int64_t rows_per_cta = ((N + grid - 1) / grid + kRows - 1) / kRows * kRows;
   cudaLaunchAttribute attr;
   const cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kThreads), smem, stream, &attr);
   return cudaLaunchKernelEx(&cfg, gemv_argmax_kernel<M>, static_cast<const __nv_bfloat16*>(w),
@@ -290,19 +301,17 @@ int lm_head_impl(const void* weight, const void* x, int64_t M, int64_t K, int64_
     }
     cudaMemsetAsync(keys, 0, kMaxTok * sizeof(unsigned long long), stream);
   }
-  const int grid = sms * 4;
-  const int64_t rows_per_cta = ((N + grid - 1) / grid + kRows - 1) / kRows * kRows;
   auto k = argmax ? static_cast<unsigned long long*>(keys) : nullptr;
   cudaError_t e;
   switch (M) {
-    case 1: e = launch_m<1>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 2: e = launch_m<2>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 3: e = launch_m<3>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 4: e = launch_m<4>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 5: e = launch_m<5>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 6: e = launch_m<6>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    case 7: e = launch_m<7>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;
-    default: e = launch_m<8>(weight, x, N, (int)K, logits, k, grid, rows_per_cta, stream); break;  // M == 8
+    case 1: e = launch_m<1>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 2: e = launch_m<2>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 3: e = launch_m<3>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 4: e = launch_m<4>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 5: e = launch_m<5>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 6: e = launch_m<6>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    case 7: e = launch_m<7>(weight, x, N, (int)K, logits, k, sms, stream); break;
+    default: e = launch_m<8>(weight, x, N, (int)K, logits, k, sms, stream); break;  // M == 8
   }
   if (e == cudaSuccess && argmax) {
     cudaLaunchAttribute attr;
